@@ -1,0 +1,210 @@
+"""One physical frozen backbone serving three logical roles.
+
+Parity with the reference's ``MiniMaxH3A100Model``
+(``h3_a100/model.py:154-453``): Student LoRA, Fake LoRA and Teacher (adapters
+off) share one frozen DiT; both adapter sets are trainable and owned by
+disjoint optimizers; the AdaLN bank is installed before sharding; modulations
+are precomputed per exact timestep key.  Differences by design:
+
+* the role is an explicit argument of every forward (``predict_velocity``);
+  ``role_scope`` is kept as the public context manager and for logging;
+* adapters are flat per-role buffers (``LoRAStore``), not PEFT modules;
+* sharding is this package's own runtime (``h3_a100.parallel.sharded``), with
+  the reference's unit plan: time embedder, each AdaLN projection, each
+  refiner/transformer block, root.
+"""
+
+from __future__ import annotations
+
+import contextlib
+import contextvars
+import os
+from collections.abc import Iterator
+from typing import Any
+
+import torch
+from safetensors.torch import load_file, save_file
+
+from ..config import get
+from ..parallel.sharded import ShardedProjection, ShardedUnit, link_order
+from ..utils.log import logger
+from .adaln import AdaLNCacheController, adaln_bank, adaln_controller, install_adaln_cache
+from .block import H3Block
+from .dit import DiTConfig, H3DiT
+from .lora import FAKE, STUDENT, TEACHER, TRAINABLE_ROLES, LoRALayout, LoRAStore, target_modules_supported
+
+STUDENT_ADAPTER, FAKE_ADAPTER, BASE_ROLE = STUDENT, FAKE, TEACHER
+LORA_FILE = "pytorch_lora_weights.safetensors"
+
+
+def dit_config_from(config: dict[str, Any]) -> DiTConfig:
+    model = dict(get(config, "synthetic.model", {}) or {})
+    model.setdefault("video_channels", int(get(config, "model.video_latent_channels", 16)))
+    if "audio_channels" not in model:
+        model["audio_channels"] = int(get(config, "model.audio_latent_channels", 0)) if get(
+            config, "synthetic.audio_tokens", 0) else 0
+    if "patch" not in model:
+        model["patch"] = tuple(get(config, "model.patch_size", (1, 2, 2)))
+    return DiTConfig.from_dict(model)
+
+
+class H3SharedBackbone:
+    def __init__(self, config: dict[str, Any], *, device: torch.device, kernels, comm=None) -> None:
+        self.config = config
+        self.device = device
+        self.kernels = kernels
+        self.comm = comm
+        self.dit_config = dit_config_from(config)
+        dtype_name = str(get(config, "model.transformer_param_dtype", "bf16"))
+        self.param_dtype = {"bf16": torch.bfloat16, "fp32": torch.float32, "fp16": torch.float16}[dtype_name]
+        self.base_seed = int(get(config, "synthetic.base_seed", 1234))
+        self.transformer = H3DiT(self.dit_config, dtype=self.param_dtype, device=device)
+        self.transformer.init_weights(self.base_seed)
+        self.transformer.set_kernels(kernels)
+        self._role: contextvars.ContextVar[str] = contextvars.ContextVar("h3_role", default=STUDENT)
+        self.lora: dict[str, LoRAStore] = {}
+        self.units: list[ShardedUnit] = []
+        self.projections: list[ShardedProjection] = []
+        self._ready = False
+
+    # ------------------------------------------------------------------ setup
+    def denoiser_module(self) -> H3DiT:
+        return self.transformer
+
+    def prepare_shared_backbone(self, *, student_lora: dict, fake_lora: dict, cache_enabled: bool = True,
+                                max_dynamic_cache_keys: int = 2) -> None:
+        if self._ready:
+            return
+        dit = self.transformer
+        dit.requires_grad_(False)
+        install_adaln_cache(dit, enabled=cache_enabled, max_dynamic_keys=max_dynamic_cache_keys)
+        prefixes = [b.prefix for b in dit.token_refiner.refiner_blocks] + [b.prefix for b in dit.transformer_blocks]
+        for role, lcfg in ((STUDENT, student_lora), (FAKE, fake_lora)):
+            target_modules_supported(lcfg.get("target_modules", ()))
+            rank = int(lcfg["rank"])
+            layout = LoRALayout(prefixes, self.dit_config.hidden, self.dit_config.ffn, rank)
+            seed = self.base_seed * 7919 + (1 if role == STUDENT else 2)
+            self.lora[role] = LoRAStore(role, layout, alpha=float(lcfg.get("alpha", rank)),
+                                        dtype=self.param_dtype, device=self.device, seed=seed)
+        counts = {role: store.numel() for role, store in self.lora.items()}
+        if not all(counts.values()):
+            raise RuntimeError(f"failed to build LoRA adapters: {counts}")
+        self._ready = True
+        logger.info("[h3-a100] shared backbone ready student_lora_params={} fake_lora_params={}",
+                    counts[STUDENT], counts[FAKE])
+
+    def apply_sharding(self, comm, *, block_reshard: bool = True, root_reshard: bool = False) -> None:
+        """Shard frozen weights with the reference unit plan (time MLP, AdaLN each, blocks, root)."""
+        self.comm = comm
+        dit = self.transformer
+        units = []
+        for blk in list(dit.token_refiner.refiner_blocks) + list(dit.transformer_blocks):
+            unit = ShardedUnit(blk.prefix, blk, list(H3Block.WEIGHT_NAMES), comm,
+                               reshard_after_forward=block_reshard)
+            blk.attach_unit(unit)
+            units.append(unit)
+        link_order(units)
+        self.units = units
+        bank = adaln_bank(dit)
+        if comm.world_size > 1 and bank is not None:
+            self.projections = [ShardedProjection(p, comm, self.kernels) for p in bank.projections]
+        # time embedder, embeds and heads are small: kept replicated (root unit, not resharded).
+        del root_reshard
+        torch.cuda.empty_cache() if torch.cuda.is_available() else None
+
+    def is_sharded(self) -> bool:
+        return bool(self.units) and self.units[0].world > 1
+
+    # ------------------------------------------------------------------ roles
+    def role_parameters(self, role: str) -> list[torch.Tensor]:
+        if role not in TRAINABLE_ROLES:
+            raise ValueError(f"role {role!r} has no trainable parameters")
+        return [self.lora[role].flat]
+
+    def lora_store(self, role: str) -> LoRAStore | None:
+        if role == TEACHER:
+            return None
+        if role not in self.lora:
+            raise ValueError(f"unknown role {role!r}")
+        return self.lora[role]
+
+    @contextlib.contextmanager
+    def role_scope(self, role: str) -> Iterator[None]:
+        if role not in (STUDENT, FAKE, TEACHER):
+            raise ValueError(f"unknown role {role!r}")
+        token = self._role.set(role)
+        try:
+            yield
+        finally:
+            self._role.reset(token)
+
+    def current_role(self) -> str:
+        return self._role.get()
+
+    # ------------------------------------------------------------------ AdaLN
+    def adaln_cache(self) -> AdaLNCacheController:
+        controller = adaln_controller(self.transformer)
+        if controller is None:
+            raise RuntimeError("AdaLN cache was not installed")
+        return controller
+
+    @contextlib.contextmanager
+    def adaln_scope(self, key: Any, *, persistent: bool = False) -> Iterator[None]:
+        with self.adaln_cache().scope(key, persistent=persistent):
+            yield
+
+    @torch.no_grad()
+    def precompute_adaln(self, key: Any, timesteps: torch.Tensor, *, persistent: bool) -> None:
+        """Materialise every block's modulation for one exact timestep table."""
+        dit = self.transformer
+        bank = adaln_bank(dit)
+        controller = self.adaln_cache()
+        if bank is None:
+            raise RuntimeError("AdaLN projection bank is missing")
+        if controller.has_complete_key(key, len(bank.projections)):
+            return
+        temb = dit.time_embedding(timesteps.to(self.device))
+        hidden = self.dit_config.hidden
+        with controller.scope(key, persistent=persistent):
+            for index, projection in enumerate(bank.projections):
+                if self.projections:
+                    sharded = self.projections[index]
+                    fn = lambda t, s=sharded: s(t).view(t.shape[0], 6, hidden)  # noqa: E731
+                else:
+                    fn = projection
+                controller.get_or_compute(index, temb, fn)
+
+    def drop_adaln_key(self, key: Any) -> None:
+        self.adaln_cache().drop(key)
+
+    def log_adaln_stats(self, prefix: str = "[h3-a100]") -> None:
+        s = self.adaln_cache().stats()
+        logger.info("{} AdaLN cache hits={} misses={} stores={} evictions={} persistent_keys={} "
+                    "dynamic_keys={} memory_mib={:.2f}", prefix, s.hits, s.misses, s.stores, s.evictions,
+                    s.persistent_keys, s.dynamic_keys, s.bytes / 1024**2)
+
+    # ------------------------------------------------------------------ forward
+    def predict_velocity(self, role: str, latents, timesteps: torch.Tensor, condition: dict, *, adaln_key=None):
+        video, audio = latents
+        with self.role_scope(role):
+            return self.transformer(video, audio, condition["text"], timesteps,
+                                    lora_store=self.lora_store(role), adaln_key=adaln_key,
+                                    controller=self.adaln_cache())
+
+    # ------------------------------------------------------------------ LoRA IO
+    def save_all_role_loras(self, student_dir: str, fake_dir: str, *, main_process: bool = True) -> None:
+        """Rank 0 writes both roles in Diffusers key format (adapters are replicated)."""
+        if not main_process:
+            return
+        for role, out in ((STUDENT, student_dir), (FAKE, fake_dir)):
+            os.makedirs(out, exist_ok=True)
+            save_file(self.lora[role].state_dict(), os.path.join(out, LORA_FILE))
+
+    def load_role_lora(self, load_dir: str, role: str) -> None:
+        state = load_file(os.path.join(load_dir, LORA_FILE))
+        self.lora[role].load_state_dict(state)
+
+    def memory_report(self) -> dict[str, int]:
+        frozen_local = sum(u.local_bytes() for u in self.units) + sum(p.local_bytes() for p in self.projections)
+        lora = {role: s.flat.numel() * s.flat.element_size() for role, s in self.lora.items()}
+        return {"frozen_local_bytes": int(frozen_local), **{f"lora_{k}_bytes": v for k, v in lora.items()}}
