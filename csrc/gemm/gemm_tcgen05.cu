@@ -1,0 +1,615 @@
+// Persistent tcgen05 GEMM for sm_100a with fused epilogues.
+//
+//   D[M, N] = epilogue( op(A)[M, K] * op(B)[N, K]^T  (+ A2[M, K2] * B2[N, K2]^T) )
+//
+// * A, B are bf16, each K-major (row = one M/N index, K contiguous) or
+//   MN-major (row = one K index, M/N contiguous); accumulation is fp32 in
+//   tensor memory (TMEM).
+// * The optional second K-phase is how LoRA is fused: forward
+//   y = x W^T + (s x A^T) B^T runs as one accumulation over K = in + r, with
+//   the r-phase reading U = s x A^T and B.  For the fused QKV the second
+//   phase is sectioned: output columns of section s read U[:, s*r:(s+1)*r].
+// * Warp roles (192 threads, one CTA per SM, persistent over tiles):
+//     warp 0      TMA producer (one elected thread), STAGES-deep smem ring
+//     warp 1      MMA issuer (one elected thread), tcgen05.mma 128 x BN x 16
+//     warps 2..5  epilogue: tcgen05.ld from TMEM -> registers -> global
+//   TMEM holds two BN-column accumulators so the epilogue of tile i overlaps
+//   the MMAs of tile i+1.
+// * Tiles are rastered in groups of `group_m` M-tiles so the CTAs in flight
+//   share both operand panels in L2.
+// * All waits are bounded (see ptx.cuh); on a timeout the kernel records an
+//   error code, drains its own TMA loads / MMAs, frees TMEM and returns.
+// * No TMA load in this file uses cluster multicast.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cudaTypedefs.h>
+#include <torch/extension.h>
+
+#include <atomic>
+#include <mutex>
+
+#include "../common/ptx.cuh"
+#include "gemm.h"
+
+namespace h3 {
+
+std::atomic<uint64_t> g_launches{0};
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int kThreads = 192;
+
+struct GemmParams {
+  int M, N;
+  int tiles_m, tiles_n, splits;
+  int kb_main, kb_second, kb_per_split;
+  int section_n;
+  int group_m;
+  void* out;
+  long ldo;
+  void* out2;
+  long ldo2;
+  const __nv_bfloat16* bias;
+  const __nv_bfloat16* res;
+  long ldr;
+  const float* gate;
+  long ldg;
+  int split_row;
+  const float* cos_t;
+  const float* sin_t;
+  int rope_cols;
+  int head_dim;
+  const __nv_bfloat16* pre;
+  long ldp;
+  float alpha;
+  KernelStatus status;
+};
+
+template <int BN>
+struct Cfg {
+  static constexpr int kStages = (BN == 256) ? 4 : 6;
+  static constexpr int kABytes = BM * BK * 2;
+  static constexpr int kBBytes = BN * BK * 2;
+  static constexpr int kTmemCols = 2 * BN;
+  static constexpr int kSmem = 1024 + kStages * (kABytes + kBBytes) + 256;
+};
+
+__device__ __forceinline__ float gelu_tanh_f(float x) {
+  const float k0 = 0.7978845608028654f;  // sqrt(2/pi)
+  const float inner = k0 * (x + 0.044715f * x * x * x);
+  return 0.5f * x * (1.0f + tanhf(inner));
+}
+
+__device__ __forceinline__ float gelu_tanh_grad_f(float x) {
+  const float k0 = 0.7978845608028654f;
+  const float inner = k0 * (x + 0.044715f * x * x * x);
+  const float th = tanhf(inner);
+  return 0.5f * (1.0f + th) + 0.5f * x * (1.0f - th * th) * k0 * (1.0f + 3.0f * 0.044715f * x * x);
+}
+
+__device__ __forceinline__ void tile_coords(const GemmParams& p, int work, int& m_blk, int& n_blk, int& ks) {
+  ks = work % p.splits;
+  const int tile = work / p.splits;
+  const int group_size = p.group_m * p.tiles_n;
+  const int g = tile / group_size;
+  const int first_m = g * p.group_m;
+  const int gm = min(p.tiles_m - first_m, p.group_m);
+  const int in_group = tile % group_size;
+  m_blk = first_m + in_group % gm;
+  n_blk = in_group / gm;
+}
+
+// Store 16 consecutive bf16 values of one row, with an N bound.
+__device__ __forceinline__ void store_row16_bf16(__nv_bfloat16* dst, const float (&v)[16], int valid) {
+  if (valid >= 16 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+    uint4 a, b;
+    a.x = pack_bf16x2(v[0], v[1]);
+    a.y = pack_bf16x2(v[2], v[3]);
+    a.z = pack_bf16x2(v[4], v[5]);
+    a.w = pack_bf16x2(v[6], v[7]);
+    b.x = pack_bf16x2(v[8], v[9]);
+    b.y = pack_bf16x2(v[10], v[11]);
+    b.z = pack_bf16x2(v[12], v[13]);
+    b.w = pack_bf16x2(v[14], v[15]);
+    reinterpret_cast<uint4*>(dst)[0] = a;
+    reinterpret_cast<uint4*>(dst)[1] = b;
+  } else {
+    for (int j = 0; j < 16 && j < valid; ++j) dst[j] = __float2bfloat16(v[j]);
+  }
+}
+
+__device__ __forceinline__ void load_row16_bf16(const __nv_bfloat16* src, float (&v)[16], int valid) {
+  if (valid >= 16 && (reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
+    const uint4 a = reinterpret_cast<const uint4*>(src)[0];
+    const uint4 b = reinterpret_cast<const uint4*>(src)[1];
+    const __nv_bfloat16* pa = reinterpret_cast<const __nv_bfloat16*>(&a);
+    const __nv_bfloat16* pb = reinterpret_cast<const __nv_bfloat16*>(&b);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      v[j] = __bfloat162float(pa[j]);
+      v[8 + j] = __bfloat162float(pb[j]);
+    }
+  } else {
+    for (int j = 0; j < 16; ++j) v[j] = (j < valid) ? __bfloat162float(src[j]) : 0.0f;
+  }
+}
+
+template <int EPI>
+__device__ __forceinline__ void epilogue16(const GemmParams& p, int m, int n, const uint32_t (&r)[16]) {
+  const int valid = min(16, p.N - n);
+  if (valid <= 0) return;
+  float v[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+
+  if constexpr (EPI == kEpiF32Acc) {
+    float* dst = reinterpret_cast<float*>(p.out) + static_cast<long>(m) * p.ldo + n;
+    if (p.splits > 1) {
+      for (int j = 0; j < valid; ++j) atomicAdd(dst + j, p.alpha * v[j]);
+    } else {
+      for (int j = 0; j < valid; ++j) dst[j] += p.alpha * v[j];
+    }
+    return;
+  } else {
+    float bias[16];
+    if (p.bias != nullptr) {
+      load_row16_bf16(p.bias + n, bias, valid);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) bias[j] = 0.0f;
+    }
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<long>(m) * p.ldo + n;
+    if constexpr (EPI == kEpiBf16) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] = p.alpha * v[j] + bias[j];
+      store_row16_bf16(dst, v, valid);
+    } else if constexpr (EPI == kEpiGelu) {
+      float g[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        v[j] = bf16_round(v[j] + bias[j]);
+        g[j] = gelu_tanh_f(v[j]);
+      }
+      store_row16_bf16(dst, v, valid);
+      store_row16_bf16(reinterpret_cast<__nv_bfloat16*>(p.out2) + static_cast<long>(m) * p.ldo2 + n, g, valid);
+    } else if constexpr (EPI == kEpiRope) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] = bf16_round(v[j] + bias[j]);
+      if (n < p.rope_cols) {
+        const int half = p.head_dim >> 1;
+        const float* cs = p.cos_t + static_cast<long>(m) * half;
+        const float* sn = p.sin_t + static_cast<long>(m) * half;
+#pragma unroll
+        for (int j = 0; j < 16; j += 2) {
+          const int pi = ((n + j) % p.head_dim) >> 1;
+          const float c = cs[pi], s = sn[pi];
+          const float a = v[j], b = v[j + 1];
+          v[j] = a * c - b * s;
+          v[j + 1] = a * s + b * c;
+        }
+      }
+      store_row16_bf16(dst, v, valid);
+    } else if constexpr (EPI == kEpiGatedRes) {
+      float res[16];
+      load_row16_bf16(p.res + static_cast<long>(m) * p.ldr + n, res, valid);
+      const float* gate = p.gate + (m >= p.split_row ? p.ldg : 0) + n;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const float y = bf16_round(v[j] + bias[j]);
+        v[j] = res[j] + (j < valid ? gate[j] : 0.0f) * y;
+      }
+      store_row16_bf16(dst, v, valid);
+    } else if constexpr (EPI == kEpiGeluBwd) {
+      float pre[16];
+      load_row16_bf16(p.pre + static_cast<long>(m) * p.ldp + n, pre, valid);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] = bf16_round(v[j]) * gelu_tanh_grad_f(pre[j]);
+      store_row16_bf16(dst, v, valid);
+    }
+  }
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmA2a, const __grid_constant__ CUtensorMap tmA2b,
+                const __grid_constant__ CUtensorMap tmA2c, const __grid_constant__ CUtensorMap tmB2,
+                const GemmParams p) {
+  using C = Cfg<BN>;
+  constexpr int S = C::kStages;
+  constexpr uint32_t kIdesc = umma_idesc_bf16(BM, BN, A_MN, B_MN);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + S * C::kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + S * C::kBBytes);
+  uint64_t* empty = full + S;
+  uint64_t* acc_full = empty + S;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    if (p.kb_second > 0) {
+      tma_prefetch_desc(&tmA2a);
+      tma_prefetch_desc(&tmB2);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint64_t limit = p.status.limit_ns;
+  const int total_work = p.tiles_m * p.tiles_n * p.splits;
+  const int total_kb = p.kb_main + p.kb_second;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_phase[S];
+      bool issued[S];
+      for (int s = 0; s < S; ++s) issued[s] = false;
+      for (int work = blockIdx.x; work < total_work && !*abort_flag; work += gridDim.x) {
+        int m_blk, n_blk, ks;
+        tile_coords(p, work, m_blk, n_blk, ks);
+        const int m0 = m_blk * BM, n0 = n_blk * BN;
+        const int kb_lo = ks * p.kb_per_split;
+        const int kb_hi = min(total_kb, kb_lo + p.kb_per_split);
+        const CUtensorMap* a2 = &tmA2a;
+        if (p.section_n > 0) {
+          const int sec = n0 / p.section_n;
+          a2 = sec == 0 ? &tmA2a : (sec == 1 ? &tmA2b : &tmA2c);
+        }
+        for (int kb = kb_lo; kb < kb_hi; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, limit, abort_flag)) {
+            report_status(p.status, kStatusTimeoutEmpty, kb);
+            *abort_flag = 1;
+            break;
+          }
+          uint8_t* a_dst = sA + stage * C::kABytes;
+          uint8_t* b_dst = sB + stage * C::kBBytes;
+          mbar_arrive_expect_tx(&full[stage], C::kABytes + C::kBBytes);
+          if (kb < p.kb_main) {
+            const int k0 = kb * BK;
+            if constexpr (!A_MN) {
+              tma_load_2d(a_dst, &tmA, &full[stage], k0, m0);
+            } else {
+#pragma unroll
+              for (int c = 0; c < BM / 64; ++c) tma_load_2d(a_dst + c * 8192, &tmA, &full[stage], m0 + c * 64, k0);
+            }
+            if constexpr (!B_MN) {
+              tma_load_2d(b_dst, &tmB, &full[stage], k0, n0);
+            } else {
+#pragma unroll
+              for (int c = 0; c < BN / 64; ++c) tma_load_2d(b_dst + c * 8192, &tmB, &full[stage], n0 + c * 64, k0);
+            }
+          } else {
+            const int k0 = (kb - p.kb_main) * BK;
+            tma_load_2d(a_dst, a2, &full[stage], k0, m0);
+            if constexpr (!B_MN) {
+              tma_load_2d(b_dst, &tmB2, &full[stage], k0, n0);
+            } else {
+#pragma unroll
+              for (int c = 0; c < BN / 64; ++c) tma_load_2d(b_dst + c * 8192, &tmB2, &full[stage], n0 + c * 64, k0);
+            }
+          }
+          issued[stage] = true;
+          issued_phase[stage] = phase;
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Never leave a TMA write in flight into this CTA's shared memory.
+      for (int s = 0; s < S; ++s) {
+        if (issued[s] && !mbar_wait(&full[s], issued_phase[s], limit, abort_flag)) {
+          // Abort path: wait again without the abort short-cut, still bounded.
+          volatile int never = 0;
+          mbar_wait(&full[s], issued_phase[s], limit, &never);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool any = false;
+      for (int work = blockIdx.x; work < total_work && !*abort_flag; work += gridDim.x) {
+        int m_blk, n_blk, ks;
+        tile_coords(p, work, m_blk, n_blk, ks);
+        const int kb_lo = ks * p.kb_per_split;
+        const int kb_hi = min(total_kb, kb_lo + p.kb_per_split);
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, limit, abort_flag)) {
+          report_status(p.status, kStatusTimeoutAccEmpty, work);
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        bool ok = true;
+        for (int kb = kb_lo; kb < kb_hi; ++kb) {
+          if (!mbar_wait(&full[stage], phase, limit, abort_flag)) {
+            report_status(p.status, kStatusTimeoutFull, kb);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + stage * C::kABytes);
+          const uint32_t b_base = smem_u32(sB + stage * C::kBBytes);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = A_MN ? umma_smem_desc(a_base + kk * 2048, 8192, 1024)
+                                     : umma_smem_desc(a_base + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? umma_smem_desc(b_base + kk * 2048, 8192, 1024)
+                                     : umma_smem_desc(b_base + kk * 32, 16, 1024);
+            umma_f16_ss(d_tmem, ad, bd, kIdesc, (kb > kb_lo || kk > 0) ? 1u : 0u);
+          }
+          any = true;
+          umma_commit(&empty[stage]);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&acc_full[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      if (any) {
+        // Wait for every issued MMA before TMEM can be released.
+        umma_commit(drain);
+        volatile int never = 0;
+        mbar_wait(drain, 0, limit, &never);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int work = blockIdx.x; work < total_work; work += gridDim.x) {
+      int m_blk, n_blk, ks;
+      tile_coords(p, work, m_blk, n_blk, ks);
+      if (!mbar_wait(&acc_full[acc], acc_phase, limit, abort_flag)) {
+        if (lane == 0) report_status(p.status, kStatusTimeoutAccFull, work);
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int m = m_blk * BM + row;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r0[16], r1[16];
+        tmem_ld16(t_row + c, r0);
+        tmem_ld16(t_row + c + 16, r1);
+        tmem_ld_wait();
+        if (m < p.M) {
+          const int n = n_blk * BN + c;
+          epilogue16<EPI>(p, m, n, r0);
+          epilogue16<EPI>(p, m, n + 16, r1);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q);
+    TORCH_CHECK(ptr != nullptr && q == cudaDriverEntryPointSuccess, "cuTensorMapEncodeTiled not available");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// Row-major bf16 matrix [rows, cols] with row stride `ld` elements; box = {64, box_rows}.
+CUtensorMap make_map(const void* base, long rows, long cols, long ld, int box_rows) {
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(base) & 15u) == 0, "TMA base address must be 16-byte aligned");
+  TORCH_CHECK((ld * 2) % 16 == 0, "TMA row stride must be a multiple of 16 bytes (ld=", ld, ")");
+  TORCH_CHECK(rows >= 1 && cols >= 1, "empty TMA operand");
+  CUtensorMap map;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
+  cuuint32_t box[2] = {64u, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", static_cast<int>(r));
+  return map;
+}
+
+int num_sms(int device) {
+  static int cached[64] = {0};
+  if (cached[device] == 0) {
+    cudaDeviceProp prop;
+    cudaGetDeviceProperties(&prop, device);
+    cached[device] = prop.multiProcessorCount;
+  }
+  return cached[device];
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+void launch_variant(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& a2a, const CUtensorMap& a2b,
+                    const CUtensorMap& a2c, const CUtensorMap& b2, const GemmParams& p, int device,
+                    cudaStream_t stream) {
+  auto kernel = gemm_kernel<BN, A_MN, B_MN, EPI>;
+  static bool configured[64] = {false};
+  if (!configured[device]) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::kSmem);
+    configured[device] = true;
+  }
+  const int work = p.tiles_m * p.tiles_n * p.splits;
+  const int grid = std::min(work, num_sms(device));
+  kernel<<<grid, kThreads, Cfg<BN>::kSmem, stream>>>(a, b, a2a, a2b, a2c, b2, p);
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace
+
+uint64_t launch_count() { return g_launches.load(); }
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+// Operand view: base pointer, logical rows x cols of the *stored* row-major matrix, row stride.
+struct Operand {
+  const void* ptr;
+  long rows, cols, ld;
+};
+
+static Operand operand_of(const at::Tensor& t) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16, "GEMM operands must be CUDA bf16");
+  TORCH_CHECK(t.dim() == 2 && t.stride(1) == 1, "GEMM operands must be 2-D with unit column stride");
+  return {t.data_ptr(), t.size(0), t.size(1), t.stride(0)};
+}
+
+void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, int64_t M, int64_t N, int64_t K,
+          const std::vector<at::Tensor>& A2, const c10::optional<at::Tensor>& B2, int64_t K2, int64_t section_n,
+          int64_t epi, const at::Tensor& out, const c10::optional<at::Tensor>& out2,
+          const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& res,
+          const c10::optional<at::Tensor>& gate, int64_t split_row, const c10::optional<at::Tensor>& cos_t,
+          const c10::optional<at::Tensor>& sin_t, int64_t rope_cols, int64_t head_dim,
+          const c10::optional<at::Tensor>& pre, double alpha, int64_t splits, int64_t block_n,
+          const at::Tensor& status, int64_t limit_ns) {
+  const int device = A.get_device();
+  c10::cuda::CUDAGuard guard(device);
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream(device).stream();
+  TORCH_CHECK(M > 0 && N > 0 && K > 0, "GEMM sizes must be positive");
+  const int bn = static_cast<int>(block_n);
+  TORCH_CHECK(bn == 128 || bn == 256, "block_n must be 128 or 256");
+  TORCH_CHECK(!(a_mn && K2 > 0), "the second K-phase needs a K-major A");
+
+  Operand oa = operand_of(A), ob = operand_of(B);
+  // Stored shapes: K-major A = [M, K]; MN-major A = [K, M]; same for B with N.
+  CUtensorMap ma = a_mn ? make_map(oa.ptr, oa.rows, oa.cols, oa.ld, 64) : make_map(oa.ptr, oa.rows, oa.cols, oa.ld, BM);
+  CUtensorMap mb = b_mn ? make_map(ob.ptr, ob.rows, ob.cols, ob.ld, 64) : make_map(ob.ptr, ob.rows, ob.cols, ob.ld, bn);
+  CUtensorMap ma2[3] = {ma, ma, ma};
+  CUtensorMap mb2 = mb;
+  int kb_second = 0;
+  if (K2 > 0) {
+    TORCH_CHECK(!A2.empty() && A2.size() <= 3 && B2.has_value(), "second K-phase needs A2 (1..3 sections) and B2");
+    for (size_t i = 0; i < A2.size(); ++i) {
+      Operand o = operand_of(A2[i]);
+      ma2[i] = make_map(o.ptr, o.rows, o.cols, o.ld, BM);
+    }
+    for (size_t i = A2.size(); i < 3; ++i) ma2[i] = ma2[0];
+    Operand o2 = operand_of(*B2);
+    mb2 = b_mn ? make_map(o2.ptr, o2.rows, o2.cols, o2.ld, 64) : make_map(o2.ptr, o2.rows, o2.cols, o2.ld, bn);
+    kb_second = static_cast<int>((K2 + BK - 1) / BK);
+  }
+  GemmParams p{};
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.tiles_m = static_cast<int>((M + BM - 1) / BM);
+  p.tiles_n = static_cast<int>((N + bn - 1) / bn);
+  p.kb_main = static_cast<int>((K + BK - 1) / BK);
+  p.kb_second = kb_second;
+  const int total_kb = p.kb_main + p.kb_second;
+  int sp = std::max<int64_t>(1, std::min<int64_t>(splits, total_kb));
+  p.kb_per_split = (total_kb + sp - 1) / sp;
+  p.splits = (total_kb + p.kb_per_split - 1) / p.kb_per_split;
+  TORCH_CHECK(p.splits == 1 || epi == kEpiF32Acc, "split-K needs the fp32 accumulate epilogue");
+  TORCH_CHECK(section_n == 0 || section_n % bn == 0, "a LoRA section (", section_n,
+              " columns) must be a multiple of block_n=", bn);
+  p.section_n = static_cast<int>(section_n);
+  p.group_m = 16;
+  p.out = out.data_ptr();
+  p.ldo = out.stride(0);
+  p.out2 = out2.has_value() ? out2->data_ptr() : nullptr;
+  p.ldo2 = out2.has_value() ? out2->stride(0) : 0;
+  p.bias = bias.has_value() ? reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr()) : nullptr;
+  p.res = res.has_value() ? reinterpret_cast<const __nv_bfloat16*>(res->data_ptr()) : nullptr;
+  p.ldr = res.has_value() ? res->stride(0) : 0;
+  p.gate = gate.has_value() ? gate->data_ptr<float>() : nullptr;
+  p.ldg = gate.has_value() ? gate->stride(0) : 0;
+  p.split_row = static_cast<int>(split_row);
+  p.cos_t = cos_t.has_value() ? cos_t->data_ptr<float>() : nullptr;
+  p.sin_t = sin_t.has_value() ? sin_t->data_ptr<float>() : nullptr;
+  p.rope_cols = static_cast<int>(rope_cols);
+  p.head_dim = static_cast<int>(head_dim);
+  p.pre = pre.has_value() ? reinterpret_cast<const __nv_bfloat16*>(pre->data_ptr()) : nullptr;
+  p.ldp = pre.has_value() ? pre->stride(0) : 0;
+  p.alpha = static_cast<float>(alpha);
+  p.status.word = status.data_ptr<int>();
+  p.status.limit_ns = static_cast<uint64_t>(limit_ns);
+
+  if (epi == kEpiF32Acc) {
+    TORCH_CHECK(out.scalar_type() == at::kFloat, "fp32 accumulate epilogue needs an fp32 out");
+  } else {
+    TORCH_CHECK(out.scalar_type() == at::kBFloat16, "bf16 epilogues need a bf16 out");
+  }
+  if (epi == kEpiGatedRes) TORCH_CHECK(res.has_value() && gate.has_value(), "gated residual needs res and gate");
+  if (epi == kEpiRope) TORCH_CHECK(cos_t.has_value() && sin_t.has_value() && head_dim % 16 == 0, "rope tables");
+  if (epi == kEpiGelu) TORCH_CHECK(out2.has_value(), "gelu epilogue needs out2");
+  if (epi == kEpiGeluBwd) TORCH_CHECK(pre.has_value(), "gelu backward epilogue needs pre");
+
+#define H3_GEMM_CASE(BN_, AMN_, BMN_, EPI_)                                                   \
+  if (bn == BN_ && a_mn == AMN_ && b_mn == BMN_ && epi == EPI_) {                             \
+    launch_variant<BN_, AMN_, BMN_, EPI_>(ma, mb, ma2[0], ma2[1], ma2[2], mb2, p, device, stream); \
+    return;                                                                                   \
+  }
+  H3_GEMM_CASE(256, false, false, kEpiBf16)
+  H3_GEMM_CASE(256, false, false, kEpiRope)
+  H3_GEMM_CASE(256, false, false, kEpiGelu)
+  H3_GEMM_CASE(256, false, false, kEpiGatedRes)
+  H3_GEMM_CASE(128, false, false, kEpiBf16)
+  H3_GEMM_CASE(256, false, true, kEpiBf16)
+  H3_GEMM_CASE(256, false, true, kEpiGeluBwd)
+  H3_GEMM_CASE(128, false, true, kEpiBf16)
+  H3_GEMM_CASE(128, true, true, kEpiF32Acc)
+  H3_GEMM_CASE(256, true, true, kEpiF32Acc)
+#undef H3_GEMM_CASE
+  TORCH_CHECK(false, "no GEMM variant for block_n=", bn, " a_mn=", a_mn, " b_mn=", b_mn, " epi=", epi);
+}
+
+}  // namespace h3

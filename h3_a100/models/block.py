@@ -50,23 +50,23 @@ def block_forward(ctx: BlockContext, x: torch.Tensor, w: dict[str, torch.Tensor]
     K, mod, split, lo, s = ctx.kernels, ctx.modulation, ctx.split, ctx.lora, ctx.lora_scale
 
     def down(name, inp):
-        return K.lora_down(inp, lo[name][0]) if lo is not None else None
+        return K.lora_down(inp, lo[name][0], s) if lo is not None else None
 
     def up(name):
         return lo[name][1] if lo is not None else None
 
     h1 = K.norm_modulate(x, mod[:, SHIFT_MSA], mod[:, SCALE_MSA], split, ctx.eps)
     u_qkv = down("qkv", h1)
-    qkv = K.linear(h1, w["qkv_weight"], w["qkv_bias"], u_qkv, up("qkv"), s, 3, epilogue=ctx.rope)
+    qkv = K.linear(h1, w["qkv_weight"], w["qkv_bias"], u_qkv, up("qkv"), 3, epilogue=ctx.rope)
     o, lse = K.attention_fwd(qkv, ctx.heads, ctx.head_dim)
     u_o = down("o", o)
-    x1 = K.linear(o, w["out_weight"], w["out_bias"], u_o, up("o"), s, 1,
+    x1 = K.linear(o, w["out_weight"], w["out_bias"], u_o, up("o"), 1,
                   epilogue=GatedResidual(x, mod[:, GATE_MSA], split))
     h2 = K.norm_modulate(x1, mod[:, SHIFT_MLP], mod[:, SCALE_MLP], split, ctx.eps)
     u_f0 = down("ff0", h2)
-    pre, act = K.linear(h2, w["ff0_weight"], w["ff0_bias"], u_f0, up("ff0"), s, 1, epilogue="gelu")
+    pre, act = K.linear(h2, w["ff0_weight"], w["ff0_bias"], u_f0, up("ff0"), 1, epilogue="gelu")
     u_f2 = down("ff2", act)
-    out = K.linear(act, w["ff2_weight"], w["ff2_bias"], u_f2, up("ff2"), s, 1,
+    out = K.linear(act, w["ff2_weight"], w["ff2_bias"], u_f2, up("ff2"), 1,
                    epilogue=GatedResidual(x1, mod[:, GATE_MLP], split))
     if not save:
         return out, None
@@ -79,33 +79,32 @@ def block_backward(ctx: BlockContext, dout: torch.Tensor, w: dict[str, torch.Ten
     K, mod, split, lo, s, sinks = ctx.kernels, ctx.modulation, ctx.split, ctx.lora, ctx.lora_scale, ctx.grad_sinks
 
     def lora_part(name, dy, inp, u, sections):
-        """LoRA gradients of one linear; returns dyb for the input-gradient GEMM."""
+        """LoRA gradients of one linear; returns (s*dy*B, A_cat) for the input-gradient GEMM."""
         if lo is None:
             return None, None
         a_cat, b_cat = lo[name]
-        dyb = K.lora_dyb(dy, b_cat, sections)
+        dyb = K.lora_dyb(dy, b_cat, sections, s)
         if sinks is not None:
-            K.lora_wgrad(dy, inp, u, dyb, s, sections, sinks[name][0], sinks[name][1])
+            K.lora_wgrad(dy, inp, u, dyb, sections, sinks[name][0], sinks[name][1])
         return dyb, a_cat
 
-    # FF2 with gated residual: out = x1 + g_mlp * y2
+    # FF2 with gated residual: out = x1 + g_mlp * y2;  y2 = GELU(pre) W2^T + ...
     dy2 = K.gate_mul(dout, mod[:, GATE_MLP], split)
     dyb, a_cat = lora_part("ff2", dy2, sv["act"], sv["u_f2"], 1)
-    dact = K.linear_dx(dy2, w["ff2_weight"], dyb, a_cat, s)
-    dpre = K.gelu_bwd(dact, sv["pre"])
+    dpre = K.linear_dx(dy2, w["ff2_weight"], dyb, a_cat, gelu_pre=sv["pre"])
     dyb, a_cat = lora_part("ff0", dpre, sv["h2"], sv["u_f0"], 1)
-    dh2 = K.linear_dx(dpre, w["ff0_weight"], dyb, a_cat, s)
-    dx1 = dout + K.norm_modulate_bwd(sv["x1"], dh2, mod[:, SCALE_MLP], split, ctx.eps)
-    # O-proj with gated residual: x1 = x + g_msa * y_o
-    dyo = K.gate_mul(dx1, mod[:, GATE_MSA], split)
+    dh2 = K.linear_dx(dpre, w["ff0_weight"], dyb, a_cat)
+    # x1 feeds the MLP norm and the residual; its gradient also gives the O-proj branch (x1 = x + g_msa * y_o).
+    dx1, dyo = K.norm_modulate_bwd(sv["x1"], dh2, mod[:, SCALE_MLP], split, ctx.eps, add=dout,
+                                   gate=mod[:, GATE_MSA])
     dyb, a_cat = lora_part("o", dyo, sv["o"], sv["u_o"], 1)
-    do = K.linear_dx(dyo, w["out_weight"], dyb, a_cat, s)
+    do = K.linear_dx(dyo, w["out_weight"], dyb, a_cat)
     dqkv = K.attention_bwd(sv["qkv"], sv["o"], sv["lse"], do, ctx.heads, ctx.head_dim)
     if ctx.rope is not None:
         dqkv = K.rope_bwd(dqkv, ctx.rope)
     dyb, a_cat = lora_part("qkv", dqkv, sv["h1"], sv["u_qkv"], 3)
-    dh1 = K.linear_dx(dqkv, w["qkv_weight"], dyb, a_cat, s)
-    return dx1 + K.norm_modulate_bwd(sv["x"], dh1, mod[:, SCALE_MSA], split, ctx.eps)
+    dh1 = K.linear_dx(dqkv, w["qkv_weight"], dyb, a_cat)
+    return K.norm_modulate_bwd(sv["x"], dh1, mod[:, SCALE_MSA], split, ctx.eps, add=dx1)
 
 
 class _BlockFn(torch.autograd.Function):

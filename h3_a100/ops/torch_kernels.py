@@ -14,7 +14,10 @@ Conventions shared with the native kernels (``h3_a100/ops/native.py``):
   row 1 (video+text tokens come first, audio tokens last);
 * LoRA for a linear with S output sections (the fused QKV has 3) is stored as
   ``A_cat [S*r, in]`` and ``B_cat [out, r]``; section ``s`` of the output uses
-  rows ``s*r:(s+1)*r`` of ``A_cat`` and its own rows of ``B_cat``;
+  rows ``s*r:(s+1)*r`` of ``A_cat`` and its own rows of ``B_cat``.  The LoRA
+  scale ``s = alpha/r`` is applied exactly once, in ``lora_down``
+  (``U = s * x A^T``) and in ``lora_dyb`` (``dyb = s * dy B``); every other
+  LoRA term uses those scaled tensors;
 * RoPE rotates interleaved pairs ``(2i, 2i+1)`` of every head with per-token
   tables ``cos, sin: [T, head_dim/2]`` (fp32).
 """
@@ -94,29 +97,35 @@ class TorchKernels:
         y = xf * r * (1.0 + _rows(x.shape[0], split, scale)) + _rows(x.shape[0], split, shift)
         return y.to(x.dtype)
 
-    def norm_modulate_bwd(self, x, dy, scale, split, eps=1e-6):
+    def norm_modulate_bwd(self, x, dy, scale, split, eps=1e-6, add=None, gate=None):
+        """dx = add + d(norm_modulate)/dx^T dy; with ``gate`` also returns gate[row] * dx."""
         xf, g = x.float(), dy.float() * (1.0 + _rows(x.shape[0], split, scale))
         r = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
         n = xf * r
         dx = r * (g - n * (g * n).mean(-1, keepdim=True))
-        return dx.to(x.dtype)
+        if add is not None:
+            dx = dx + add.float()
+        dx = dx.to(x.dtype)
+        if gate is None:
+            return dx
+        return dx, (dx.float() * _rows(x.shape[0], split, gate)).to(x.dtype)
 
     # ---------------- linear layers with LoRA ----------------
-    def lora_down(self, x, a_cat):
-        return (x.float() @ a_cat.float().t()).to(x.dtype)
+    def lora_down(self, x, a_cat, scale=1.0):
+        return (scale * (x.float() @ a_cat.float().t())).to(x.dtype)
 
-    def _lora_up(self, y, u, b_cat, lora_scale, sections):
+    def _lora_up(self, y, u, b_cat, sections):
         n = y.shape[1]
         r = u.shape[1] // sections
         width = n // sections
         for s in range(sections):
-            y[:, s * width:(s + 1) * width] += lora_scale * (
+            y[:, s * width:(s + 1) * width] += (
                 u[:, s * r:(s + 1) * r].float() @ b_cat[s * width:(s + 1) * width].float().t()
             )
         return y
 
-    def linear(self, x, w, b=None, u=None, b_cat=None, lora_scale=1.0, sections=1, epilogue=None):
-        """y = x w^T + b (+ LoRA up) then the epilogue.
+    def linear(self, x, w, b=None, u=None, b_cat=None, sections=1, epilogue=None):
+        """y = x w^T + b (+ U B^T, the LoRA up-projection) then the epilogue.
 
         epilogue: None | "gelu" (returns (pre, post)) | Rope | GatedResidual.
         """
@@ -127,7 +136,7 @@ class TorchKernels:
         else:
             y = (torch.addmm(b, x, w.t()) if b is not None else x @ w.t()).float()
         if u is not None:
-            y = self._lora_up(y, u, b_cat, lora_scale, sections)
+            y = self._lora_up(y, u, b_cat, sections)
         if epilogue is None:
             return y.to(x.dtype)
         if epilogue == "gelu":
@@ -140,27 +149,34 @@ class TorchKernels:
             return (epilogue.residual.float() + gate * y.to(x.dtype).float()).to(x.dtype)
         raise ValueError(f"unknown epilogue {epilogue!r}")
 
-    def lora_dyb(self, dy, b_cat, sections):
+    def lora_dyb(self, dy, b_cat, sections, scale=1.0):
         n = dy.shape[1]
         width = n // sections
         parts = [dy[:, s * width:(s + 1) * width].float() @ b_cat[s * width:(s + 1) * width].float()
                  for s in range(sections)]
-        return torch.cat(parts, 1).to(dy.dtype)
+        return (scale * torch.cat(parts, 1)).to(dy.dtype)
 
-    def linear_dx(self, dy, w, dyb=None, a_cat=None, lora_scale=1.0):
-        dx = dy.float() @ w.float()
+    def linear_dx(self, dy, w, dyb=None, a_cat=None, gelu_pre=None):
+        """dx = dy w + dyb A_cat; with ``gelu_pre`` also applies the GELU derivative."""
+        if dy.dtype == torch.float32:
+            dx = dy @ w
+        else:
+            dx = (dy @ w).float()
         if dyb is not None:
-            dx = dx + lora_scale * (dyb.float() @ a_cat.float())
-        return dx.to(dy.dtype)
+            dx = dx + dyb.float() @ a_cat.float()
+        dx = dx.to(dy.dtype)
+        if gelu_pre is not None:
+            dx = self.gelu_bwd(dx, gelu_pre)
+        return dx
 
-    def lora_wgrad(self, dy, x, u, dyb, lora_scale, sections, grad_a, grad_b):
-        """Accumulate dA_cat = s*dyb^T x and dB_s = s*dy_s^T u_s into fp32 sinks."""
-        grad_a += lora_scale * (dyb.float().t() @ x.float())
+    def lora_wgrad(self, dy, x, u, dyb, sections, grad_a, grad_b):
+        """Accumulate dA_cat = dyb^T x and dB_s = dy_s^T U_s into the fp32 sinks."""
+        grad_a += dyb.float().t() @ x.float()
         n = dy.shape[1]
         width = n // sections
         r = u.shape[1] // sections
         for s in range(sections):
-            grad_b[s * width:(s + 1) * width] += lora_scale * (
+            grad_b[s * width:(s + 1) * width] += (
                 dy[:, s * width:(s + 1) * width].float().t() @ u[:, s * r:(s + 1) * r].float()
             )
 

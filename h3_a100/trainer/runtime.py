@@ -37,7 +37,7 @@ class PreparedFakeUpdate:
     generated: tuple[torch.Tensor, torch.Tensor | None]
     noises: tuple[torch.Tensor, torch.Tensor | None]
     renoised: tuple[torch.Tensor, torch.Tensor | None]
-    sigmas: tuple[torch.Tensor, torch.Tensor]
+    sigmas: tuple[float, float]
     cache_key: tuple[str, int]
 
 
@@ -53,13 +53,13 @@ class DMDRuntimeMixin:
             return int(self.matched_fixed_end_step_idx)
         return int(torch.randint(int(low), int(high), (1,), generator=self.host_rng).item())
 
-    def _sample_renoise_sigmas(self) -> tuple[torch.Tensor, torch.Tensor]:
+    def _sample_renoise_sigmas(self) -> tuple[float, float]:
         u = torch.empty(1).uniform_(self.renoise_sigma_min, self.renoise_sigma_max, generator=self.host_rng)
-        return (shift_sigma(u, self.video_flow_shift).to(self.device),
-                shift_sigma(u, self.audio_flow_shift).to(self.device))
+        return float(shift_sigma(u, self.video_flow_shift)), float(shift_sigma(u, self.audio_flow_shift))
 
     def _timesteps(self, sigmas) -> torch.Tensor:
-        return torch.stack([sigmas[0].reshape(()), sigmas[1].reshape(())]).float() * self.num_train_timesteps
+        t = torch.tensor([float(sigmas[0]), float(sigmas[1])], dtype=torch.float32) * self.num_train_timesteps
+        return t.to(self.device, non_blocking=True)
 
     def sample_initial_latents(self, latent_shape) -> tuple[torch.Tensor, torch.Tensor | None]:
         video = torch.randn(latent_shape["video"], device=self.device, dtype=torch.float32).to(self.latent_dtype)
@@ -91,8 +91,8 @@ class DMDRuntimeMixin:
             xt = self.sample_initial_latents(latent_shape)
         x0, backward_key = None, None
         for step in range(end_step_idx + 1):
-            sig = (self.video_sigmas_cpu[step].to(self.device), self.audio_sigmas_cpu[step].to(self.device))
-            nxt = (self.video_sigmas_cpu[step + 1].to(self.device), self.audio_sigmas_cpu[step + 1].to(self.device))
+            sig = (float(self.video_sigmas_cpu[step]), float(self.audio_sigmas_cpu[step]))
+            nxt = (float(self.video_sigmas_cpu[step + 1]), float(self.audio_sigmas_cpu[step + 1]))
             key = ("rollout", int(step))
             self.model.precompute_adaln(key, self._timesteps(sig), persistent=True)
             with_grad = grad_enabled and step == end_step_idx

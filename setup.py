@@ -1,0 +1,41 @@
+"""Builds the sm_100a extension in-tree: ``python setup.py build_ext --inplace``.
+
+Produces ``h3_a100/_C.*.so``.  Only ``sm_100a`` code is generated (tcgen05,
+TMA and TMEM instructions exist only there).
+"""
+
+import os
+
+os.environ.setdefault("TORCH_CUDA_ARCH_LIST", "10.0a")
+
+from setuptools import setup  # noqa: E402
+from torch.utils.cpp_extension import BuildExtension, CUDAExtension  # noqa: E402
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+SOURCES = [
+    "csrc/bindings.cpp",
+    "csrc/gemm/gemm_tcgen05.cu",
+    "csrc/elementwise/elementwise.cu",
+    "csrc/staging/pinned_pool.cpp",
+]
+NVCC_FLAGS = [
+    "-O3",
+    "-std=c++17",
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-lineinfo",
+    "--expt-relaxed-constexpr",
+    "-Xptxas", "-v" if os.environ.get("H3_PTXAS_VERBOSE") else "-O3",
+]
+
+setup(
+    name="h3_a100_b200_ext",
+    ext_modules=[
+        CUDAExtension(
+            name="h3_a100._C",
+            sources=[os.path.join(ROOT, s) for s in SOURCES],
+            include_dirs=[os.path.join(ROOT, "csrc")],
+            extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
+        )
+    ],
+    cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
+)
