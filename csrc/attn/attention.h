@@ -1,0 +1,13 @@
+// Host API of the tcgen05 attention kernels.
+#pragma once
+#include <torch/extension.h>
+
+#include <vector>
+
+namespace h3 {
+
+// qkv [T, 3H] bf16 (RoPE applied) -> {o [T, H] bf16, lse [heads, T] fp32 (natural log)}
+std::vector<at::Tensor> attention_fwd(const at::Tensor& qkv, int64_t heads, int64_t head_dim, const at::Tensor& status,
+                                      int64_t limit_ns);
+
+}  // namespace h3

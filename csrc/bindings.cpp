@@ -1,6 +1,7 @@
 // Python bindings of the sm_100a extension (module h3_a100._C).
 #include <torch/extension.h>
 
+#include "attn/attention.h"
 #include "elementwise/elementwise.h"
 #include "gemm/gemm.h"
 
@@ -12,6 +13,7 @@ int64_t pinned_bytes();
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "Hand-written sm_100a kernels of the H3 DMD trainer";
   m.def("gemm", &h3::gemm, "tcgen05 GEMM with fused epilogues");
+  m.def("attention_fwd", &h3::attention_fwd, "tcgen05 attention forward");
   m.def("launch_count", &h3::launch_count, "number of kernels launched by this extension");
   m.def("norm_modulate_fwd", &h3::norm_modulate_fwd);
   m.def("norm_modulate_bwd", &h3::norm_modulate_bwd);

@@ -499,6 +499,9 @@ void launch_variant(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMa
 }  // namespace
 
 uint64_t launch_count() { return g_launches.load(); }
+
+// 2-D bf16 tensor map with a {64, 128} box and 128-byte swizzle (used by attention).
+CUtensorMap attn_map_2d(const void* base, long rows, long cols, long ld) { return make_map(base, rows, cols, ld, 128); }
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 // Operand view: base pointer, logical rows x cols of the *stored* row-major matrix, row stride.

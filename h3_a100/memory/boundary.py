@@ -70,6 +70,15 @@ def _alias(t: torch.Tensor):
             tuple(t.shape), tuple(t.stride()), str(t.dtype))
 
 
+def _pinned_empty(numel: int, dtype: torch.dtype) -> torch.Tensor:
+    """Exact-size pinned buffer (the native allocator; torch's rounds up to a power of two)."""
+    try:
+        from .. import _C
+    except ImportError:
+        return torch.empty(numel, dtype=dtype, pin_memory=True)
+    return _C.pinned_empty(numel, dtype)
+
+
 class PinnedSlabPool:
     """Reusable host buffers keyed by (bytes, dtype); pinned when requested."""
 
@@ -95,7 +104,7 @@ class PinnedSlabPool:
             self._sweep()
             if self._free[key]:
                 return self._free[key].pop()
-        slab = torch.empty(int(numel), dtype=dtype, pin_memory=self.pin_memory)
+        slab = _pinned_empty(int(numel), dtype) if self.pin_memory else torch.empty(int(numel), dtype=dtype)
         self.allocated_bytes += slab.numel() * slab.element_size()
         return slab
 
@@ -171,6 +180,7 @@ class BoundaryStager:
         if staged.upload is not None:
             return
         stream = self._copy_stream(staged.device)
+        self.stats["prefetch_count"] += 1
         if stream is None:
             staged.upload = staged.slab.clone()
             return
@@ -182,7 +192,6 @@ class BoundaryStager:
             staged.h2d_done = torch.cuda.Event()
             staged.h2d_done.record(stream)
         staged.upload.record_stream(stream)
-        self.stats["prefetch_count"] += 1
 
     def stage_in(self, staged: _Staged) -> torch.Tensor:
         self._start_upload(staged)

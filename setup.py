@@ -16,6 +16,7 @@ SOURCES = [
     "csrc/bindings.cpp",
     "csrc/gemm/gemm_tcgen05.cu",
     "csrc/elementwise/elementwise.cu",
+    "csrc/attn/attention_fwd.cu",
     "csrc/staging/pinned_pool.cpp",
 ]
 NVCC_FLAGS = [

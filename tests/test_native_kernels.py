@@ -231,3 +231,31 @@ def test_block_forward_backward_matches_oracle(K):
         close(sink_n[name][0], sink_r[name][0], 5e-2)
         close(sink_n[name][1], sink_r[name][1], 5e-2)
     K.check_status()
+
+
+@pytest.mark.parametrize("t,heads", [(300, 2), (1000, 3), (128, 1)])
+def test_attention_forward_matches_oracle(K, t, heads):
+    if not K.attention_native:
+        pytest.skip("extension built without the tcgen05 attention")
+    torch.manual_seed(12)
+    hd = 128
+    qkv = bf(t, 3 * heads * hd)
+    o, lse = K.attention_fwd(qkv, heads, hd)
+    o_r, lse_r = R.attention_fwd(qkv.float(), heads, hd)
+    close(o, o_r, 3e-2)
+    close(lse, lse_r, 1e-3)
+    K.check_status()
+
+
+def test_attention_forward_large_logits(K):
+    """Rows whose max grows across KV tiles exercise the lazy O rescaling."""
+    if not K.attention_native:
+        pytest.skip("extension built without the tcgen05 attention")
+    torch.manual_seed(13)
+    t, heads, hd = 700, 2, 128
+    qkv = bf(t, 3 * heads * hd, scale=4.0)
+    o, lse = K.attention_fwd(qkv, heads, hd)
+    o_r, lse_r = R.attention_fwd(qkv.float(), heads, hd)
+    close(o, o_r, 3e-2)
+    close(lse, lse_r, 2e-3)
+    K.check_status()
