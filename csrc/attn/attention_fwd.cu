@@ -4,20 +4,25 @@
 //
 // q, k, v are read in place from the fused QKV output [T, 3H] (bf16, RoPE
 // already applied by the QKV GEMM epilogue); o is [T, H] bf16, lse fp32.
-// Head dim D = 128.  One CTA per (128-query tile, head), 192 threads:
-//   warp 0      TMA: Q once, then K_j / V_j into a 2-stage ring
-//   warp 1      tcgen05.mma issuer (one thread):
-//                 S_j  = Q K_j^T   (128 x 128, into TMEM S[j % 2])
-//                 O   += P_j V_j   (128 x 128, TMEM accumulator; P_j from smem)
-//               S_{j+1} is issued before waiting for P_j, so the next QK^T
-//               overlaps the current softmax.
-//   warps 2..5  softmax, one query row per thread: tcgen05.ld of S_j,
-//               running max / sum in base 2, P_j (bf16) written to smem in the
-//               128-byte-swizzled K-major layout the MMA reads.  The O
-//               accumulator is rescaled in TMEM only when some row's max grew
-//               by more than 2^8 (the exponent base is allowed to lag the true
-//               max by that much); the decision is warp-uniform because
-//               tcgen05.ld/st are warp-collective.
+// Head dim D = 128.
+//
+// One CTA per (pair of 128-query tiles, head), 320 threads:
+//   warp 0      TMA: Q_0, Q_1 once, then K_j / V_j into a 2-stage ring
+//   warp 1      tcgen05.mma issuer (one thread), per KV tile j:
+//                 S_t = Q_t K_j^T         into TMEM S_t (t = 0, 1)
+//                 O_t += P_t V_j          P_t read from TMEM (the .ts form),
+//                                         O_t accumulates in TMEM
+//               issue order S_0 S_1 | PV_0 S_0' PV_1 S_1' | ..., so the tensor
+//               core works on one query tile while the other tile's softmax runs.
+//   warps 2..5  softmax of query tile 0, warps 6..9 of query tile 1; one query
+//               row per thread.  Pass 1 streams S_t from TMEM for the row max;
+//               pass 2 streams it again, computes 2^(s - m), accumulates the
+//               row sum and writes P as packed bf16 pairs back into the first
+//               64 TMEM columns of S_t (already consumed), where the PV MMA
+//               reads it.  O_t is rescaled in TMEM only when some row's max
+//               grew by more than 2^8 (warp-uniform decision: tcgen05.ld/st
+//               are warp-collective).
+// TMEM: S_0 [0,128) S_1 [128,256) O_0 [256,384) O_1 [384,512) fp32 columns.
 // Keys past T are masked to -inf; queries past T are computed and not stored.
 // Every wait is bounded (see ptx.cuh).  No TMA load uses cluster multicast.
 #include <ATen/cuda/CUDAContext.h>
@@ -31,18 +36,18 @@
 
 namespace h3 {
 CUtensorMap attn_map_2d(const void* base, long rows, long cols, long ld);
-int attn_num_sms(int device);
 
 namespace {
 
 constexpr int kBQ = 128;
 constexpr int kBKV = 128;
 constexpr int kD = 128;
-constexpr int kThreads = 192;
-constexpr int kChunk = 128 * 64 * 2;  // 128 rows x 64 bf16 (one 128B-swizzled column chunk)
+constexpr int kQTiles = 2;
+constexpr int kThreads = 64 + kQTiles * 128;
+constexpr int kChunk = 128 * 64 * 2;    // 128 rows x 64 bf16 (one 128B-swizzled column chunk)
 constexpr int kTileBytes = 2 * kChunk;  // 128 rows x 128 bf16
-constexpr int kSmem = 1024 + kTileBytes * 6 + 512;  // Q, K[2], V[2], P
-constexpr float kRescaleThreshold = 8.0f;          // log2 units
+constexpr int kSmem = 1024 + kTileBytes * (kQTiles + 4) + 512;  // Q x2, K[2], V[2]
+constexpr float kRescaleThreshold = 8.0f;                      // log2 units
 
 struct FwdParams {
   int T, H;
@@ -59,32 +64,106 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// 2^x on the FMA pipe, to take part of the exponentials off the MUFU unit:
+// x = n + f with n = round(x) (magic-number add, no conversion instruction)
+// and f in [-1/2, 1/2]; 2^f is a cubic least-squares fit at Chebyshev nodes
+// (max relative error 1.0e-4, below bf16 resolution); 2^n is added to the
+// exponent field.  Valid for x >= -126 (inputs are clamped).
+__device__ __forceinline__ float exp2_fma(float x) {
+  x = fmaxf(x, -126.0f);
+  const float magic = 12582912.0f;  // 1.5 * 2^23
+  const float t = x + magic;
+  const int n = __float_as_int(t) - 0x4B400000;
+  const float f = x - (t - magic);
+  float p = fmaf(0.05592203512787819f, f, 0.24264007806777954f);
+  p = fmaf(p, f, 0.6931210160255432f);
+  p = fmaf(p, f, 0.9999244809150696f);
+  return __int_as_float(__float_as_int(p) + (n << 23));
+}
+
+// 32 lanes x 32 bit, 32 consecutive columns per thread.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+// Row max of one 128-key S tile streamed from TMEM (raw scores; masked past `valid`).
+template <bool MASKED>
+__device__ __forceinline__ float row_max(uint32_t tS, int valid) {
+  float m = -INFINITY;
+#pragma unroll
+  for (int c = 0; c < kBKV / 32; ++c) {
+    uint32_t r[32];
+    tmem_ld32(tS + c * 32, r);
+    tmem_ld_wait();
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float v = __uint_as_float(r[i]);
+      m = fmaxf(m, (!MASKED || c * 32 + i < valid) ? v : -INFINITY);
+    }
+  }
+  return m;
+}
+
+// Writes P = 2^(s*scale - m) as packed bf16 pairs over the consumed S columns; returns the row sum.
+template <bool MASKED>
+__device__ __forceinline__ float row_exp_pack(uint32_t tS, int valid, float scale, float m) {
+  float sum = 0.f;
+#pragma unroll
+  for (int c = 0; c < kBKV / 32; ++c) {
+    uint32_t r[32];
+    tmem_ld32(tS + c * 32, r);
+    tmem_ld_wait();
+    uint32_t packed[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float xa = fmaf(__uint_as_float(r[2 * i]), scale, -m);
+      const float xb = fmaf(__uint_as_float(r[2 * i + 1]), scale, -m);
+      // one pair in four goes through the FMA-pipe exponential
+      float a = (i & 3) == 3 ? exp2_fma(xa) : ex2(xa);
+      float b = (i & 3) == 3 ? exp2_fma(xb) : ex2(xb);
+      if (MASKED) {
+        const int k0 = c * 32 + 2 * i;
+        a = k0 < valid ? a : 0.f;
+        b = k0 + 1 < valid ? b : 0.f;
+      }
+      sum += a + b;
+      packed[i] = pack_bf16x2(a, b);
+    }
+    tmem_st16(tS + c * 16, packed);
+  }
+  return sum;
+}
 
 __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_constant__ CUtensorMap tm, FwdParams p) {
   constexpr uint32_t kIdescS = umma_idesc_bf16(kBQ, kBKV, false, false);
   constexpr uint32_t kIdescPV = umma_idesc_bf16(kBQ, kD, false, true);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = sQ + kTileBytes;        // 2 stages
-  uint8_t* sV = sK + 2 * kTileBytes;    // 2 stages
-  uint8_t* sP = sV + 2 * kTileBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kTileBytes);
+  uint8_t* sQ = smem;                        // kQTiles tiles
+  uint8_t* sK = sQ + kQTiles * kTileBytes;   // 2 stages
+  uint8_t* sV = sK + 2 * kTileBytes;         // 2 stages
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + 2 * kTileBytes);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;    // [2]
-  uint64_t* kv_empty = bars + 3;   // [2]
-  uint64_t* s_full = bars + 5;     // [2]
-  uint64_t* s_empty = bars + 7;    // [2]
-  uint64_t* p_full = bars + 9;
-  uint64_t* o_done = bars + 10;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;    // [kQTiles]
+  uint64_t* p_full = bars + 7;    // [kQTiles]
+  uint64_t* o_done = bars + 9;    // [kQTiles]
   uint64_t* drain = bars + 11;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id(), lane = lane_id();
-  const int q_tile = blockIdx.x, head = blockIdx.y;
-  const int q0 = q_tile * kBQ;
+  const int head = blockIdx.y;
+  const int q0 = blockIdx.x * (kQTiles * kBQ);
   const int n_kv = p.n_kv;
   const uint64_t limit = p.status.limit_ns;
 
@@ -93,11 +172,12 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     for (int i = 0; i < 2; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
-      mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 128);
     }
-    mbar_init(p_full, 128);
-    mbar_init(o_done, 1);
+    for (int t = 0; t < kQTiles; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 128);
+      mbar_init(&o_done[t], 1);
+    }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -111,16 +191,17 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS[2] = {tmem, tmem + 128};
-  const uint32_t tO = tmem + 256;
 
   if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
     if (elect_one()) {
       const int xq = head * kD, xk = p.H + head * kD, xv = 2 * p.H + head * kD;
-      mbar_arrive_expect_tx(q_full, kTileBytes);
-      tma_load_2d(sQ, &tm, q_full, xq, q0);
-      tma_load_2d(sQ + kChunk, &tm, q_full, xq + 64, q0);
-      int issued_stage_phase[2] = {-1, -1};
+      mbar_arrive_expect_tx(q_full, kQTiles * kTileBytes);
+      for (int t = 0; t < kQTiles; ++t) {
+        tma_load_2d(sQ + t * kTileBytes, &tm, q_full, xq, q0 + t * kBQ);
+        tma_load_2d(sQ + t * kTileBytes + kChunk, &tm, q_full, xq + 64, q0 + t * kBQ);
+      }
+      int issued_phase[2] = {-1, -1};
       for (int j = 0; j < n_kv && !*abort_flag; ++j) {
         const int st = j & 1;
         const uint32_t ph = (j >> 1) & 1;
@@ -135,55 +216,66 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         tma_load_2d(sK + st * kTileBytes + kChunk, &tm, &kv_full[st], xk + 64, y);
         tma_load_2d(sV + st * kTileBytes, &tm, &kv_full[st], xv, y);
         tma_load_2d(sV + st * kTileBytes + kChunk, &tm, &kv_full[st], xv + 64, y);
-        issued_stage_phase[st] = static_cast<int>(ph);
+        issued_phase[st] = static_cast<int>(ph);
       }
       volatile int never = 0;
       mbar_wait(q_full, 0, limit, &never);
       for (int st = 0; st < 2; ++st)
-        if (issued_stage_phase[st] >= 0) mbar_wait(&kv_full[st], issued_stage_phase[st], limit, &never);
+        if (issued_phase[st] >= 0) mbar_wait(&kv_full[st], issued_phase[st], limit, &never);
     }
   } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
     if (elect_one()) {
       bool any = false;
       bool ok = mbar_wait(q_full, 0, limit, abort_flag);
-      auto issue_s = [&](int j) -> bool {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&kv_full[st], ph, limit, abort_flag)) return false;
-        if (!mbar_wait(&s_empty[st], ph ^ 1u, limit, abort_flag)) return false;
-        tc_fence_after();
-        const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK + st * kTileBytes);
+      auto issue_s = [&](int t, int j) {
+        const uint32_t q_base = smem_u32(sQ + t * kTileBytes), k_base = smem_u32(sK + (j & 1) * kTileBytes);
 #pragma unroll
         for (int ds = 0; ds < kD / 16; ++ds) {
           const uint32_t off = (ds >> 2) * kChunk + (ds & 3) * 32;
-          umma_f16_ss(tS[st], umma_smem_desc(q_base + off, 16, 1024), umma_smem_desc(k_base + off, 16, 1024), kIdescS,
-                      ds > 0 ? 1u : 0u);
+          umma_f16_ss(tmem + t * 128, umma_smem_desc(q_base + off, 16, 1024), umma_smem_desc(k_base + off, 16, 1024),
+                      kIdescS, ds > 0 ? 1u : 0u);
         }
-        umma_commit(&s_full[st]);
+        umma_commit(&s_full[t]);
         any = true;
-        return true;
       };
-      if (ok) ok = issue_s(0);
-      for (int j = 0; ok && j < n_kv; ++j) {
-        if (j + 1 < n_kv && !issue_s(j + 1)) {
-          ok = false;
-          break;
-        }
-        if (!mbar_wait(p_full, j & 1, limit, abort_flag)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const int st = j & 1;
-        const uint32_t p_base = smem_u32(sP), v_base = smem_u32(sV + st * kTileBytes);
+      auto issue_pv = [&](int t, int j) {
+        const uint32_t v_base = smem_u32(sV + (j & 1) * kTileBytes);
+        const uint32_t p_tmem = tmem + t * 128;          // packed bf16 P in the first 64 S columns
+        const uint32_t o_tmem = tmem + 256 + t * 128;
 #pragma unroll
         for (int ks = 0; ks < kBKV / 16; ++ks) {
-          const uint64_t a = umma_smem_desc(p_base + (ks >> 2) * kChunk + (ks & 3) * 32, 16, 1024);
-          const uint64_t b = umma_smem_desc(v_base + ks * 2048, kChunk, 1024);
-          umma_f16_ss(tO, a, b, kIdescPV, (j > 0 || ks > 0) ? 1u : 0u);
+          umma_f16_ts(o_tmem, p_tmem + ks * 8, umma_smem_desc(v_base + ks * 2048, kChunk, 1024), kIdescPV,
+                      (j > 0 || ks > 0) ? 1u : 0u);
         }
-        umma_commit(o_done);
-        umma_commit(&kv_empty[st]);
+        umma_commit(&o_done[t]);
+      };
+      if (ok && n_kv > 0) {
+        ok = mbar_wait(&kv_full[0], 0, limit, abort_flag);
+        if (ok) {
+          tc_fence_after();
+          for (int t = 0; t < kQTiles; ++t) issue_s(t, 0);
+        }
+      }
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const bool more = j + 1 < n_kv;
+        for (int t = 0; t < kQTiles && ok; ++t) {
+          if (!mbar_wait(&p_full[t], j & 1, limit, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_pv(t, j);
+          if (t == kQTiles - 1) umma_commit(&kv_empty[j & 1]);
+          if (more) {
+            if (t == 0 && !mbar_wait(&kv_full[(j + 1) & 1], ((j + 1) >> 1) & 1, limit, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_s(t, j + 1);
+          }
+        }
       }
       if (!ok) {
         report_status(p.status, kStatusTimeoutFull, blockIdx.x);
@@ -196,37 +288,25 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       }
     }
   } else {
-    // ------------------------------------------------------------ softmax
-    const int quarter = warp & 3;
+    // ------------------------------------------------------------ softmax (two warpgroups)
+    const int t = (warp - 2) >> 2;           // query tile handled by this warpgroup
+    const int quarter = warp & 3;            // TMEM lane quarter this warp may access
     const int row = quarter * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t tS = tmem + t * 128 + lane_off;
+    const uint32_t tO = tmem + 256 + t * 128 + lane_off;
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
-      const int sb = j & 1;
-      if (!mbar_wait(&s_full[sb], (j >> 1) & 1, limit, abort_flag)) {
+      if (!mbar_wait(&s_full[t], j & 1, limit, abort_flag)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float s[kBKV];
-#pragma unroll
-      for (int c = 0; c < kBKV / 16; ++c) {
-        uint32_t r[16];
-        tmem_ld16(tS[sb] + lane_off + c * 16, r);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) s[c * 16 + i] = __uint_as_float(r[i]);
-      }
-      tmem_ld_wait();
-      tc_fence_before();
-      mbar_arrive(&s_empty[sb]);
       const int kv_valid = p.T - j * kBKV;
-      float m_tile = -INFINITY;
-#pragma unroll
-      for (int i = 0; i < kBKV; ++i) {
-        s[i] = (i < kv_valid) ? s[i] * p.scale_log2 : -INFINITY;
-        m_tile = fmaxf(m_tile, s[i]);
-      }
+      // pass 1: row max (raw scores; the scale is positive)
+      float m_tile = kv_valid >= kBKV ? row_max<false>(tS, kv_valid) : row_max<true>(tS, kv_valid);
+      m_tile *= p.scale_log2;
       const float m_new = fmaxf(m_used, m_tile);
       const bool need = (j == 0) || (m_new > m_used + kRescaleThreshold);
       const bool warp_need = __any_sync(0xffffffffu, need);
@@ -235,56 +315,39 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         l *= alpha;
         m_used = m_new;
       }
-      // P_j = 2^(s - m_used), computed while PV_{j-1} may still be running.
-      float rowsum = 0.f;
-#pragma unroll
-      for (int i = 0; i < kBKV; ++i) {
-        s[i] = ex2(s[i] - m_used);
-        rowsum += s[i];
-      }
-      // The P buffer and the O accumulator are free once PV_{j-1} completed.
-      if (j > 0 && !mbar_wait(o_done, (j - 1) & 1, limit, abort_flag)) {
+      // O_t and the P slot are free once PV_t of the previous tile completed.
+      if (j > 0 && !mbar_wait(&o_done[t], (j - 1) & 1, limit, abort_flag)) {
         ok = false;
         break;
       }
+      tc_fence_after();
       if (warp_need && j > 0) {
-        tc_fence_after();
 #pragma unroll
         for (int c = 0; c < kD / 16; ++c) {
           uint32_t r[16];
-          tmem_ld16(tO + lane_off + c * 16, r);
+          tmem_ld16(tO + c * 16, r);
           tmem_ld_wait();
 #pragma unroll
           for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-          tmem_st16(tO + lane_off + c * 16, r);
+          tmem_st16(tO + c * 16, r);
         }
-        tmem_st_wait();
       }
-      // bf16 P rows into the 128B-swizzled K-major tile the PV MMA reads.
-#pragma unroll
-      for (int u = 0; u < kBKV / 8; ++u) {
-        uint4 packed;
-        packed.x = pack_bf16x2(s[u * 8 + 0], s[u * 8 + 1]);
-        packed.y = pack_bf16x2(s[u * 8 + 2], s[u * 8 + 3]);
-        packed.z = pack_bf16x2(s[u * 8 + 4], s[u * 8 + 5]);
-        packed.w = pack_bf16x2(s[u * 8 + 6], s[u * 8 + 7]);
-        const int chunk = u >> 3, unit = u & 7;
-        uint8_t* dst = sP + chunk * kChunk + row * 128 + ((unit ^ (row & 7)) << 4);
-        *reinterpret_cast<uint4*>(dst) = packed;
-      }
+      // pass 2: P = 2^(s*scale - m) as packed bf16 pairs over the consumed S columns.
+      const float rowsum = kv_valid >= kBKV ? row_exp_pack<false>(tS, kv_valid, p.scale_log2, m_used)
+                                            : row_exp_pack<true>(tS, kv_valid, p.scale_log2, m_used);
       l += rowsum;
-      fence_async_smem();
+      tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[t]);
     }
-    if (ok && n_kv > 0 && mbar_wait(o_done, (n_kv - 1) & 1, limit, abort_flag)) {
+    const int q = q0 + t * kBQ + row;
+    if (ok && n_kv > 0 && mbar_wait(&o_done[t], (n_kv - 1) & 1, limit, abort_flag)) {
       tc_fence_after();
-      const int q = q0 + row;
       const float inv_l = l > 0.f ? 1.f / l : 0.f;
 #pragma unroll
       for (int c = 0; c < kD / 16; ++c) {
         uint32_t r[16];
-        tmem_ld16(tO + lane_off + c * 16, r);
+        tmem_ld16(tO + c * 16, r);
         tmem_ld_wait();
         if (q < p.T) {
           uint4 a, b;
@@ -302,7 +365,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         }
       }
       if (q < p.T) p.lse[static_cast<long>(head) * p.T + q] = (m_used + __log2f(l)) * 0.6931471805599453f;
-    } else if (!ok || n_kv > 0) {
+    } else if (n_kv > 0) {
       if (lane == 0) report_status(p.status, kStatusTimeoutAccFull, blockIdx.x);
       *abort_flag = 1;
     }
@@ -346,7 +409,7 @@ std::vector<at::Tensor> attention_fwd(const at::Tensor& qkv, int64_t heads, int6
     cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
     configured[device] = true;
   }
-  dim3 grid(static_cast<unsigned>((T + kBQ - 1) / kBQ), static_cast<unsigned>(heads));
+  dim3 grid(static_cast<unsigned>((T + kQTiles * kBQ - 1) / (kQTiles * kBQ)), static_cast<unsigned>(heads));
   attn_fwd_kernel<<<grid, kThreads, kSmem, at::cuda::getCurrentCUDAStream(device).stream()>>>(tm, p);
   note_launch();
   C10_CUDA_KERNEL_LAUNCH_CHECK();
