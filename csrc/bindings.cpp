@@ -14,6 +14,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "Hand-written sm_100a kernels of the H3 DMD trainer";
   m.def("gemm", &h3::gemm, "tcgen05 GEMM with fused epilogues");
   m.def("attention_fwd", &h3::attention_fwd, "tcgen05 attention forward");
+  m.def("attention_bwd", &h3::attention_bwd, "tcgen05 attention backward");
   m.def("launch_count", &h3::launch_count, "number of kernels launched by this extension");
   m.def("norm_modulate_fwd", &h3::norm_modulate_fwd);
   m.def("norm_modulate_bwd", &h3::norm_modulate_bwd);

@@ -58,6 +58,7 @@ def main(argv=None) -> None:
     p.add_argument("--iters", type=int, default=5)
     p.add_argument("--which", default="native,torch")
     p.add_argument("--skip-attention", action="store_true")
+    p.add_argument("--only", default="", help="comma-separated op labels (prefix match) to run")
     args = p.parse_args(argv)
     from .ops.native import NativeKernels
 
@@ -109,7 +110,14 @@ def main(argv=None) -> None:
         if not args.skip_attention:
             heads = args.heads
             cases.append(("attention_fwd", lambda: K.attention_fwd(qkv, heads, hd), 4.0 * t * t * h, "flop"))
+            o_att, lse_att = K.attention_fwd(qkv, heads, hd)
+            do_att = bf(t, h)
+            cases.append(("attention_bwd", lambda: K.attention_bwd(qkv, o_att, lse_att, do_att, heads, hd),
+                          10.0 * t * t * h, "flop"))
+        only = [o for o in args.only.split(",") if o]
         for label, fn, work, kind in cases:
+            if only and not any(label.startswith(o) for o in only):
+                continue
             try:
                 ms = timeit(fn, args.iters)
             except Exception as exc:  # noqa: BLE001 - report and continue

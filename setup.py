@@ -17,6 +17,7 @@ SOURCES = [
     "csrc/gemm/gemm_tcgen05.cu",
     "csrc/elementwise/elementwise.cu",
     "csrc/attn/attention_fwd.cu",
+    "csrc/attn/attention_bwd.cu",
     "csrc/noalloc/dmd_loss_noalloc.cu",
     "csrc/staging/pinned_pool.cpp",
 ]

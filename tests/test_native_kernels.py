@@ -259,3 +259,20 @@ def test_attention_forward_large_logits(K):
     close(o, o_r, 3e-2)
     close(lse, lse_r, 2e-3)
     K.check_status()
+
+
+@pytest.mark.parametrize("t,heads", [(300, 2), (640, 1), (1000, 3)])
+def test_attention_backward_matches_oracle(K, t, heads):
+    if not hasattr(K.C, "attention_bwd"):
+        pytest.skip("extension built without the tcgen05 attention backward")
+    torch.manual_seed(14)
+    hd = 128
+    qkv = bf(t, 3 * heads * hd)
+    o, lse = K.attention_fwd(qkv, heads, hd)
+    do = bf(t, heads * hd)
+    dqkv = K.attention_bwd(qkv, o, lse, do, heads, hd)
+    dqkv_r = R.attention_bwd(qkv.float(), o.float(), None, do.float(), heads, hd)
+    h = heads * hd
+    for s in range(3):
+        close(dqkv[:, s * h:(s + 1) * h], dqkv_r[:, s * h:(s + 1) * h], 4e-2)
+    K.check_status()
