@@ -11,13 +11,17 @@
 //           tiles i:
 //             S^T  = K Q_i^T,  dP^T = V dO_i^T          (tcgen05, smem operands)
 //             P^T  = 2^(S^T*scale*log2e - lse2),  dS^T = scale * P^T (dP^T - delta)
-//                    (warps 2..5, one key row per thread; written back into TMEM
-//                    as packed bf16 and dS^T also into smem)
+//                    (warps 2..9: one key row per thread, the two warpgroups
+//                    split the query columns; written back into TMEM as packed
+//                    bf16 and dS^T also into smem; a quarter of the
+//                    exponentials run on the FMA pipe)
 //             dQ_i = dS K                               (smem A, MN-major), two
 //                    N = 64 halves in the TMEM columns S^T / dP^T leave free
 //             dV  += P^T dO_i,  dK += dS^T Q_i          (A from TMEM, .ts form)
-//           warps 6..9 read dQ_i out of TMEM while the tensor core runs the dV/dK
-//           MMAs and add it into an fp32 accumulator with vector red.global.add;
+//           the same warps then read dQ_i out of TMEM (half of it each) while the
+//           tensor core runs the dV/dK MMAs, stage it in the consumed dS^T buffer
+//           and add it into an fp32 accumulator with TMA bulk tensor reduce-adds
+//           (whole 128-byte lines; 16-byte red.add was the bottleneck);
 //           warp 0 streams Q_i, dO_i, lse2_i, delta_i (2 stages), warp 1 issues
 //           the MMAs.  dV/dK are written once at the end.
 //   finish  dq = bf16(dQ accumulator)
@@ -30,18 +34,21 @@
 #include <cudaTypedefs.h>
 #include <torch/extension.h>
 
+#include <cstdlib>
+
 #include "../common/ptx.cuh"
 #include "../gemm/gemm.h"
 #include "attention.h"
 
 namespace h3 {
 CUtensorMap attn_map_2d(const void* base, long rows, long cols, long ld);
+CUtensorMap make_map_f32(const void* base, long rows, long cols, long ld, int box_rows);
 
 namespace {
 
 constexpr int kB = 128;  // keys per CTA and queries per step
 constexpr int kD = 128;
-constexpr int kThreads = 320;
+constexpr int kThreads = 320;  // TMA, MMA, 2 x 4 softmax / dQ-reducer warps
 constexpr int kChunk = 128 * 64 * 2;
 constexpr int kTile = 2 * kChunk;                       // 128 x 128 bf16
 constexpr int kVecBytes = kB * 4;                       // 128 floats
@@ -56,6 +63,7 @@ struct BwdParams {
   const float* delta;
   float* dq_acc;           // [T, H] fp32
   __nv_bfloat16* dqkv;     // [T, 3H]
+  int ablate;              // diagnostic only (H3_ATTN_BWD_ABLATE): 1 skip dQ adds, 2 skip exponentials
   KernelStatus status;
 };
 
@@ -84,12 +92,37 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                : "memory");
 }
 
-__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
-               : "memory");
+// Bulk tensor reduce-add of one smem box into global memory (whole 128-byte lines).
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const void* smem_src, int x, int y) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+      : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+
+__device__ __forceinline__ void named_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// 2^x on the FMA pipe (round-to-nearest split, cubic least-squares fit of 2^f on
+// [-1/2, 1/2] at Chebyshev nodes, max relative error 1.0e-4); x >= -126.
+__device__ __forceinline__ float exp2_fma(float x) {
+  x = fmaxf(x, -126.0f);
+  const float magic = 12582912.0f;
+  const float t = x + magic;
+  const int n = __float_as_int(t) - 0x4B400000;
+  const float f = x - (t - magic);
+  float q = fmaf(0.05592203512787819f, f, 0.24264007806777954f);
+  q = fmaf(q, f, 0.6931210160255432f);
+  q = fmaf(q, f, 0.9999244809150696f);
+  return __int_as_float(__float_as_int(q) + (n << 23));
+}
 
 __global__ void attn_bwd_prep_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout,
                                      const float* __restrict__ lse, int T, int T_pad, int H, int heads,
@@ -131,7 +164,7 @@ __global__ void attn_bwd_finish_kernel(const float* __restrict__ dq_acc, int T, 
 
 __global__ void __launch_bounds__(kThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
-                    BwdParams p) {
+                    const __grid_constant__ CUtensorMap tm_dq, BwdParams p) {
   constexpr uint32_t kIdescSS = umma_idesc_bf16(kB, kB, false, false);     // S^T, dP^T
   constexpr uint32_t kIdescQ = umma_idesc_bf16(kB, 64, true, true);        // dQ halves
   constexpr uint32_t kIdescTS = umma_idesc_bf16(kB, kD, false, true);      // dV, dK (A in TMEM)
@@ -170,9 +203,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&qd_empty[s], 1);
     }
     mbar_init(s_full, 1);
-    mbar_init(p_full, 128);
+    mbar_init(p_full, 256);
     mbar_init(dq_full, 1);
-    mbar_init(dq_empty, 128);
+    mbar_init(dq_empty, 256);
     mbar_init(acc_done, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -181,6 +214,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tm_qkv);
     tma_prefetch_desc(&tm_do);
+    tma_prefetch_desc(&tm_dq);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
@@ -289,10 +323,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait(drain, 0, limit, &never);
       }
     }
-  } else if (warp < 6) {
-    // ------------------------------------------------------------ P^T / dS^T (one key row per thread)
+  } else {
+    // ------------------------------------------------------------ P^T / dS^T and the dQ reduction
+    // Warpgroup `half` (warps 2..5 -> 0, 6..9 -> 1) owns query columns
+    // [64*half, 64*half + 64) of every step: it loads all of its S^T / dP^T
+    // columns first, then writes P^T / dS^T as packed bf16 into columns
+    // [32*half, 32*half + 32) of the same regions.  Warpgroup 1's writes land
+    // on columns warpgroup 0 reads, so it waits on named barrier 1 until
+    // warpgroup 0's loads completed.  Afterwards each warpgroup adds half of
+    // dQ_i (d in [64*half, 64*half + 64)) into the fp32 accumulator.
     const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;  // key within the tile
+    const int half = (warp - 2) >> 2;
+    const int row = quarter * 32 + lane;  // key (softmax) or query (dQ) row within the tile
     const bool key_valid = k0 + row < p.T;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     bool ok = true;
@@ -302,21 +344,38 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const float* lse2 = reinterpret_cast<const float*>(sStage + st * kStageBytes + 2 * kTile);
       const float* delta = lse2 + kB;
+      uint32_t rs[2][32], rd[2][32];
 #pragma unroll
-      for (int c = 0; c < kB / 32; ++c) {
-        uint32_t rs[32], rd[32];
-        tmem_ld32(tS + lane_off + c * 32, rs);
-        tmem_ld32(tDP + lane_off + c * 32, rd);
-        tmem_ld_wait();
+      for (int cc = 0; cc < 2; ++cc) {
+        tmem_ld32(tS + lane_off + (half * 2 + cc) * 32, rs[cc]);
+        tmem_ld32(tDP + lane_off + (half * 2 + cc) * 32, rd[cc]);
+      }
+      tmem_ld_wait();
+      if (half == 0) {
+        asm volatile("bar.arrive 1, 256;" ::: "memory");
+      } else {
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+      }
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c = half * 2 + cc;  // 32-query chunk of the step
         uint32_t pp[16], dd[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const int q = c * 32 + 2 * j;
-          float pa = ex2(fmaf(__uint_as_float(rs[2 * j]), p.scale_log2, -lse2[q]));
-          float pb = ex2(fmaf(__uint_as_float(rs[2 * j + 1]), p.scale_log2, -lse2[q + 1]));
+          const float xa = fmaf(__uint_as_float(rs[cc][2 * j]), p.scale_log2, -lse2[q]);
+          const float xb = fmaf(__uint_as_float(rs[cc][2 * j + 1]), p.scale_log2, -lse2[q + 1]);
+          float pa, pb;
+          if (p.ablate & 2) {
+            pa = xa;
+            pb = xb;
+          } else {
+            pa = (j & 3) == 3 ? exp2_fma(xa) : ex2(xa);
+            pb = (j & 3) == 3 ? exp2_fma(xb) : ex2(xb);
+          }
           if (!key_valid) pa = pb = 0.f;
-          const float da = p.scale * pa * (__uint_as_float(rd[2 * j]) - delta[q]);
-          const float db = p.scale * pb * (__uint_as_float(rd[2 * j + 1]) - delta[q + 1]);
+          const float da = p.scale * pa * (__uint_as_float(rd[cc][2 * j]) - delta[q]);
+          const float db = p.scale * pb * (__uint_as_float(rd[cc][2 * j + 1]) - delta[q + 1]);
           pp[j] = pack_bf16x2(pa, pb);
           dd[j] = pack_bf16x2(da, db);
         }
@@ -339,69 +398,68 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(p_full);
+      // dQ_i (rows = queries): this warpgroup's 64 columns as two 32-column fp32
+      // boxes, staged in its 16 KB half of the (now consumed) dS^T buffer in the
+      // 128B-swizzled layout and added into the accumulator by a TMA bulk reduce.
+      if (!mbar_wait(dq_full, i & 1, limit, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      {
+        uint8_t* stage = sDS + half * (kTile / 2);
+        const uint32_t src = (half == 0 ? tS : tDP) + 64 + lane_off;
+#pragma unroll
+        for (int box = 0; box < 2; ++box) {
+          uint32_t r[32];
+          tmem_ld32(src + box * 32, r);
+          tmem_ld_wait();
+          if (!(p.ablate & 1)) {
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              uint4 v;
+              v.x = r[u * 4];
+              v.y = r[u * 4 + 1];
+              v.z = r[u * 4 + 2];
+              v.w = r[u * 4 + 3];
+              *reinterpret_cast<uint4*>(stage + row * 128 + ((u ^ (row & 7)) << 4)) = v;
+            }
+            fence_async_smem();
+            named_sync(2 + half, 128);
+            if (quarter == 0 && lane == 0) {
+              tma_reduce_add_2d(&tm_dq, stage, head * kD + half * 64 + box * 32, i * kB);
+              bulk_wait_read_all();
+            }
+            named_sync(2 + half, 128);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(dq_empty);
     }
-    // final dV, dK rows -> dqkv
+    // final dV (warpgroup 0) / dK (warpgroup 1) rows -> dqkv
     if (ok && n_q > 0 && mbar_wait(acc_done, 0, limit, abort_flag)) {
       tc_fence_after();
       const long key = k0 + row;
+      const uint32_t src = (half == 0 ? tDV : tDK) + lane_off;
+      __nv_bfloat16* dst = p.dqkv + key * 3 * p.H + (half == 0 ? 2 : 1) * p.H + head * kD;
 #pragma unroll
-      for (int which = 0; which < 2; ++which) {
-        const uint32_t src = (which == 0 ? tDV : tDK) + lane_off;
-        __nv_bfloat16* dst = p.dqkv + key * 3 * p.H + (which == 0 ? 2 : 1) * p.H + head * kD;
+      for (int c = 0; c < kD / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(src + c * 32, r);
+        tmem_ld_wait();
+        if (key_valid) {
 #pragma unroll
-        for (int c = 0; c < kD / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(src + c * 32, r);
-          tmem_ld_wait();
-          if (key_valid) {
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              uint4 v;
-              v.x = pack_bf16x2(__uint_as_float(r[u * 8 + 0]), __uint_as_float(r[u * 8 + 1]));
-              v.y = pack_bf16x2(__uint_as_float(r[u * 8 + 2]), __uint_as_float(r[u * 8 + 3]));
-              v.z = pack_bf16x2(__uint_as_float(r[u * 8 + 4]), __uint_as_float(r[u * 8 + 5]));
-              v.w = pack_bf16x2(__uint_as_float(r[u * 8 + 6]), __uint_as_float(r[u * 8 + 7]));
-              reinterpret_cast<uint4*>(dst + c * 32)[u] = v;
-            }
+          for (int u = 0; u < 4; ++u) {
+            uint4 v;
+            v.x = pack_bf16x2(__uint_as_float(r[u * 8 + 0]), __uint_as_float(r[u * 8 + 1]));
+            v.y = pack_bf16x2(__uint_as_float(r[u * 8 + 2]), __uint_as_float(r[u * 8 + 3]));
+            v.z = pack_bf16x2(__uint_as_float(r[u * 8 + 4]), __uint_as_float(r[u * 8 + 5]));
+            v.w = pack_bf16x2(__uint_as_float(r[u * 8 + 6]), __uint_as_float(r[u * 8 + 7]));
+            reinterpret_cast<uint4*>(dst + c * 32)[u] = v;
           }
         }
       }
     } else if (n_q > 0) {
       if (lane == 0) report_status(p.status, kStatusTimeoutAccFull, blockIdx.x);
       *abort_flag = 1;
-    }
-  } else {
-    // ------------------------------------------------------------ dQ_i reducers (one query row per thread)
-    const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;
-    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    for (int i = 0; i < n_q; ++i) {
-      if (!mbar_wait(dq_full, i & 1, limit, abort_flag)) {
-        if (lane == 0) report_status(p.status, kStatusTimeoutAccFull, i);
-        *abort_flag = 1;
-        break;
-      }
-      tc_fence_after();
-      const int q = i * kB + row;
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t r[32];
-        const uint32_t src = (half == 0 ? tS : tDP) + 64 + lane_off;
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          tmem_ld32(src + c * 32, r);
-          tmem_ld_wait();
-          if (q < p.T) {
-            float* dst = p.dq_acc + static_cast<long>(q) * p.H + head * kD + half * 64 + c * 32;
-#pragma unroll
-            for (int u = 0; u < 8; ++u)
-              red_add_v4(dst + u * 4, __uint_as_float(r[u * 4]), __uint_as_float(r[u * 4 + 1]),
-                         __uint_as_float(r[u * 4 + 2]), __uint_as_float(r[u * 4 + 3]));
-          }
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(dq_empty);
     }
   }
 
@@ -456,6 +514,7 @@ at::Tensor attention_bwd(const at::Tensor& qkv, const at::Tensor& o, const at::T
   p.delta = delta.data_ptr<float>();
   p.dq_acc = dq_acc.data_ptr<float>();
   p.dqkv = reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr());
+  if (const char* ab = std::getenv("H3_ATTN_BWD_ABLATE")) p.ablate = std::atoi(ab);
   p.status.word = status.data_ptr<int>();
   p.status.limit_ns = static_cast<uint64_t>(limit_ns);
   static bool configured[64] = {false};
@@ -464,7 +523,8 @@ at::Tensor attention_bwd(const at::Tensor& qkv, const at::Tensor& o, const at::T
     configured[device] = true;
   }
   dim3 grid(static_cast<unsigned>(T_pad / kB), static_cast<unsigned>(heads));
-  attn_bwd_kernel<<<grid, kThreads, kSmem, stream>>>(tm_qkv, tm_do, p);
+  CUtensorMap tm_dq = make_map_f32(dq_acc.data_ptr(), T, H, H, kB);
+  attn_bwd_kernel<<<grid, kThreads, kSmem, stream>>>(tm_qkv, tm_do, tm_dq, p);
   note_launch();
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   {

@@ -97,18 +97,15 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 // Row max of one 128-key S tile streamed from TMEM (raw scores; masked past `valid`).
 template <bool MASKED>
 __device__ __forceinline__ float row_max(uint32_t tS, int valid) {
+  uint32_t r[kBKV / 32][32];
+#pragma unroll
+  for (int c = 0; c < kBKV / 32; ++c) tmem_ld32(tS + c * 32, r[c]);  // all loads in flight, one wait
+  tmem_ld_wait();
   float m = -INFINITY;
 #pragma unroll
-  for (int c = 0; c < kBKV / 32; ++c) {
-    uint32_t r[32];
-    tmem_ld32(tS + c * 32, r);
-    tmem_ld_wait();
+  for (int c = 0; c < kBKV / 32; ++c)
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const float v = __uint_as_float(r[i]);
-      m = fmaxf(m, (!MASKED || c * 32 + i < valid) ? v : -INFINITY);
-    }
-  }
+    for (int i = 0; i < 32; ++i) m = fmaxf(m, (!MASKED || c * 32 + i < valid) ? __uint_as_float(r[c][i]) : -INFINITY);
   return m;
 }
 
@@ -117,27 +114,32 @@ template <bool MASKED>
 __device__ __forceinline__ float row_exp_pack(uint32_t tS, int valid, float scale, float m) {
   float sum = 0.f;
 #pragma unroll
-  for (int c = 0; c < kBKV / 32; ++c) {
-    uint32_t r[32];
-    tmem_ld32(tS + c * 32, r);
+  for (int cp = 0; cp < kBKV / 64; ++cp) {
+    uint32_t r[2][32];
+    tmem_ld32(tS + cp * 64, r[0]);  // two chunks in flight per wait
+    tmem_ld32(tS + cp * 64 + 32, r[1]);
     tmem_ld_wait();
-    uint32_t packed[16];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const float xa = fmaf(__uint_as_float(r[2 * i]), scale, -m);
-      const float xb = fmaf(__uint_as_float(r[2 * i + 1]), scale, -m);
-      // one pair in four goes through the FMA-pipe exponential
-      float a = (i & 3) == 3 ? exp2_fma(xa) : ex2(xa);
-      float b = (i & 3) == 3 ? exp2_fma(xb) : ex2(xb);
-      if (MASKED) {
-        const int k0 = c * 32 + 2 * i;
-        a = k0 < valid ? a : 0.f;
-        b = k0 + 1 < valid ? b : 0.f;
+    for (int h = 0; h < 2; ++h) {
+      const int c = cp * 2 + h;
+      uint32_t packed[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float xa = fmaf(__uint_as_float(r[h][2 * i]), scale, -m);
+        const float xb = fmaf(__uint_as_float(r[h][2 * i + 1]), scale, -m);
+        // one pair in four goes through the FMA-pipe exponential
+        float a = (i & 3) == 3 ? exp2_fma(xa) : ex2(xa);
+        float b = (i & 3) == 3 ? exp2_fma(xb) : ex2(xb);
+        if (MASKED) {
+          const int k0 = c * 32 + 2 * i;
+          a = k0 < valid ? a : 0.f;
+          b = k0 + 1 < valid ? b : 0.f;
+        }
+        sum += a + b;
+        packed[i] = pack_bf16x2(a, b);
       }
-      sum += a + b;
-      packed[i] = pack_bf16x2(a, b);
+      tmem_st16(tS + c * 16, packed);
     }
-    tmem_st16(tS + c * 16, packed);
   }
   return sum;
 }

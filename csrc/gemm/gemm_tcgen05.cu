@@ -502,6 +502,21 @@ uint64_t launch_count() { return g_launches.load(); }
 
 // 2-D bf16 tensor map with a {64, 128} box and 128-byte swizzle (used by attention).
 CUtensorMap attn_map_2d(const void* base, long rows, long cols, long ld) { return make_map(base, rows, cols, ld, 128); }
+
+// 2-D fp32 tensor map [rows, cols] (row stride `ld` elements), box {32, box_rows}, 128-byte swizzle.
+CUtensorMap make_map_f32(const void* base, long rows, long cols, long ld, int box_rows) {
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(base) & 15u) == 0 && (ld * 4) % 16 == 0, "fp32 TMA operand alignment");
+  CUtensorMap map;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 4)};
+  cuuint32_t box[2] = {32u, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box,
+                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (fp32) failed: ", static_cast<int>(r));
+  return map;
+}
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 // Operand view: base pointer, logical rows x cols of the *stored* row-major matrix, row stride.
