@@ -27,8 +27,8 @@
 //   finish  dq = bf16(dQ accumulator)
 // TMEM: dV [0,128) dK [128,256) S^T/P^T [256,384) dP^T/dS^T [384,512); dQ_i halves
 // in [320,384) and [448,512).  Keys past T give zero P / dS; queries past T are
-// neutralised by lse2 = +inf.  All waits are bounded; no TMA load uses cluster
-// multicast.
+// neutralised by lse2 = +inf.  All waits are bounded; every TMA load targets one
+// CTA only.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <cudaTypedefs.h>

@@ -24,7 +24,7 @@
 //               are warp-collective).
 // TMEM: S_0 [0,128) S_1 [128,256) O_0 [256,384) O_1 [384,512) fp32 columns.
 // Keys past T are masked to -inf; queries past T are computed and not stored.
-// Every wait is bounded (see ptx.cuh).  No TMA load uses cluster multicast.
+// Every wait is bounded (see ptx.cuh).  Every TMA load targets one CTA only.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <cudaTypedefs.h>

@@ -2,6 +2,7 @@
 #include <torch/extension.h>
 
 #include "attn/attention.h"
+#include "comm/p2p.h"
 #include "elementwise/elementwise.h"
 #include "gemm/gemm.h"
 
@@ -15,6 +16,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &h3::gemm, "tcgen05 GEMM with fused epilogues");
   m.def("attention_fwd", &h3::attention_fwd, "tcgen05 attention forward");
   m.def("attention_bwd", &h3::attention_bwd, "tcgen05 attention backward");
+  m.def("p2p_all_gather", &h3::p2p_all_gather, "pull all-gather over peer memory");
+  m.def("lora_rs_adamw", &h3::lora_rs_adamw, "fused LoRA reduce-scatter + clip + AdamW + all-gather");
+  m.def("adaln_project_gather", &h3::adaln_project_gather, "row-sharded AdaLN GEMV with fused output all-gather");
+  m.def("wait_flag_test", &h3::wait_flag_test, "bounded wait on a flag (failure-detection tests)");
   m.def("launch_count", &h3::launch_count, "number of kernels launched by this extension");
   m.def("norm_modulate_fwd", &h3::norm_modulate_fwd);
   m.def("norm_modulate_bwd", &h3::norm_modulate_bwd);

@@ -19,7 +19,7 @@
 //   share both operand panels in L2.
 // * All waits are bounded (see ptx.cuh); on a timeout the kernel records an
 //   error code, drains its own TMA loads / MMAs, frees TMEM and returns.
-// * No TMA load in this file uses cluster multicast.
+// * Every TMA load in this file targets one CTA only.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <cudaTypedefs.h>

@@ -97,6 +97,38 @@ def training_system_section(config: dict[str, Any]) -> dict[str, Any]:
     return training.get("a100", training.get("b200", {})) or {}
 
 
+# H3-shaped model dims used when a config has no `synthetic:` block (for
+# example the reference's own YAMLs): they reproduce the reference's logged
+# invariants (see configs/h3_dmd_b200_world8.yaml for the derivation).
+H3_MODEL_DIMS = {"hidden": 5376, "heads": 42, "head_dim": 128, "ffn": 25088, "time_embed_dim": 8064,
+                 "num_blocks": 50, "num_refiner_blocks": 2, "text_dim": 4096}
+H3_TEXT_TOKENS = 512
+H3_AUDIO_TOKENS_PER_FRAME = 5970 / 124
+
+
+def synthetic_defaults(config: dict[str, Any]) -> dict[str, Any]:
+    """`synthetic:` block derived from `model:` and `training.dmd` (canvas size, frames)."""
+    model = config.get("model", {}) or {}
+    dmd = get(config, "training.dmd", {}) or {}
+    vae = int(model.get("vae_spatial_scale_factor", 16))
+    cv, ca = int(model.get("video_latent_channels", 24)), int(model.get("audio_latent_channels", 32))
+    frames = int(dmd.get("num_frames", 124))
+    latent_frames = (frames + 3) // 4
+    audio_tokens = int(round(frames * H3_AUDIO_TOKENS_PER_FRAME))
+    seed = get(config, "training.seed", 20260817)
+    return {
+        "base_seed": int(seed),
+        "data_seed": int(seed),
+        "num_samples": 96,
+        "data_dtype": "bf16",
+        "video_latent_shape": [cv, latent_frames, int(dmd.get("height", 768)) // vae, int(dmd.get("width", 1344)) // vae],
+        "audio_latent_shape": [ca, audio_tokens] if ca else None,
+        "audio_tokens": audio_tokens if ca else 0,
+        "text_shape": [H3_TEXT_TOKENS, H3_MODEL_DIMS["text_dim"]],
+        "model": {**H3_MODEL_DIMS, "video_channels": cv, "audio_channels": ca},
+    }
+
+
 def load_config(path: str | os.PathLike[str], overrides: dict[str, Any] | None = None) -> dict[str, Any]:
     """Load, merge ``overrides`` (nested dict) and resolve a YAML config."""
     text = Path(path).read_text(encoding="utf-8")
@@ -106,6 +138,10 @@ def load_config(path: str | os.PathLike[str], overrides: dict[str, Any] | None =
     if overrides:
         config = merge(config, overrides)
     config = resolve(config)
+    if "synthetic" not in config and "training" in config:
+        config["synthetic"] = synthetic_defaults(config)
+    elif overrides and "synthetic" in overrides and "video_latent_shape" not in config.get("synthetic", {}):
+        config["synthetic"] = merge(synthetic_defaults(config), config["synthetic"])
     config.setdefault("_meta", {})["path"] = str(path)
     return config
 

@@ -114,13 +114,18 @@ class LoRAStore:
     """Flat bf16/fp32 parameters of one role plus an fp32 gradient sink."""
 
     def __init__(self, role: str, layout: LoRALayout, *, alpha: float, dtype: torch.dtype,
-                 device: torch.device, seed: int) -> None:
+                 device: torch.device, seed: int, alloc=None, pad_to: int = 1) -> None:
         if role not in TRAINABLE_ROLES:
             raise ValueError(f"role {role!r} has no adapter")
         self.role = role
         self.layout = layout
         self.scale = float(alpha) / float(layout.rank)
-        self.flat = torch.zeros(layout.numel, dtype=dtype, device=device)
+        # Flat buffers are padded (zeros) so they split evenly over ranks for the
+        # sharded optimizer; `alloc` may place them in peer-mapped memory.
+        pad_to = max(1, int(pad_to))
+        self.padded_numel = (layout.numel + pad_to - 1) // pad_to * pad_to
+        self._alloc = alloc or (lambda n, dt: torch.zeros(n, dtype=dt, device=device))
+        self.flat = self._alloc(self.padded_numel, dtype)
         self.grad: torch.Tensor | None = None
         gen = torch.Generator(device=device).manual_seed(int(seed))
         std = 1.0 / layout.rank
@@ -141,7 +146,7 @@ class LoRAStore:
 
     def ensure_grad(self) -> torch.Tensor:
         if self.grad is None:
-            self.grad = torch.zeros(self.layout.numel, dtype=torch.float32, device=self.flat.device)
+            self.grad = self._alloc(self.padded_numel, torch.float32)
         return self.grad
 
     def grad_sinks(self, block: str) -> dict[str, tuple[torch.Tensor, torch.Tensor]]:
@@ -154,6 +159,7 @@ class LoRAStore:
             self.grad.zero_()
 
     def numel(self) -> int:
+        """Number of LoRA parameters (without padding)."""
         return self.layout.numel
 
     # -- Diffusers-format state dict -------------------------------------------

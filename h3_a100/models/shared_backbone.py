@@ -72,7 +72,7 @@ class H3SharedBackbone:
         return self.transformer
 
     def prepare_shared_backbone(self, *, student_lora: dict, fake_lora: dict, cache_enabled: bool = True,
-                                max_dynamic_cache_keys: int = 2) -> None:
+                                max_dynamic_cache_keys: int = 2, alloc=None, pad_to: int = 1) -> None:
         if self._ready:
             return
         dit = self.transformer
@@ -85,7 +85,8 @@ class H3SharedBackbone:
             layout = LoRALayout(prefixes, self.dit_config.hidden, self.dit_config.ffn, rank)
             seed = self.base_seed * 7919 + (1 if role == STUDENT else 2)
             self.lora[role] = LoRAStore(role, layout, alpha=float(lcfg.get("alpha", rank)),
-                                        dtype=self.param_dtype, device=self.device, seed=seed)
+                                        dtype=self.param_dtype, device=self.device, seed=seed,
+                                        alloc=alloc, pad_to=pad_to)
         counts = {role: store.numel() for role, store in self.lora.items()}
         if not all(counts.values()):
             raise RuntimeError(f"failed to build LoRA adapters: {counts}")

@@ -39,6 +39,13 @@ class TorchComm:
         self.bytes_reduced = 0
 
     # ---------------- buffers ----------------
+    def alloc_shard(self, numel: int, dtype: torch.dtype) -> torch.Tensor:
+        return torch.empty(int(numel), dtype=dtype, device=self.device)
+
+    def alloc_symmetric(self, numel: int, dtype: torch.dtype) -> torch.Tensor:
+        """Plain (non-peer-mapped) zeroed buffer; the peer transport overrides this."""
+        return torch.zeros(int(numel), dtype=dtype, device=self.device)
+
     def _buffer(self, numel: int, dtype: torch.dtype) -> torch.Tensor:
         free = self._free[numel]
         for i, (buf, event) in enumerate(free):

@@ -70,7 +70,7 @@ class ShardedUnit:
                 full[spec.offset:spec.offset + spec.numel].copy_(p.detach().reshape(-1))
             self.shard = full
         else:
-            self.shard = torch.empty(self.shard_numel, dtype=dtype, device=device)
+            self.shard = comm.alloc_shard(self.shard_numel, dtype)
             lo, hi = self.rank * self.shard_numel, (self.rank + 1) * self.shard_numel
             for spec, p in zip(specs, params):
                 a, b = max(lo, spec.offset), min(hi, spec.offset + spec.numel)
@@ -144,6 +144,22 @@ class ShardedProjection:
         module.bias.data = torch.empty(0, dtype=b.dtype, device=b.device)
 
     def __call__(self, temb: torch.Tensor) -> torch.Tensor:
+        if hasattr(self.comm, "adaln_project") and temb.shape[0] <= 2:
+            # Fused GEMV + all-gather: every rank stores its rows into every rank's
+            # output buffer.  Two buffers alternate so a fast rank never overwrites
+            # an output a slow rank has not copied yet.
+            bufs = getattr(self.comm, "_adaln_out_buffers", None)
+            need = 2 * self.comm.world_size * self.rows
+            if bufs is None or bufs[0].numel() < need:
+                bufs = [self.comm.alloc_symmetric(need, torch.float32) for _ in range(2)]
+                self.comm._adaln_out_buffers = bufs
+                self.comm._adaln_calls = 0
+            buf = bufs[self.comm._adaln_calls % 2]
+            self.comm._adaln_calls += 1
+            r = temb.shape[0]
+            out = buf[: r * self.comm.world_size * self.rows].view(r, -1)
+            self.comm.adaln_project(temb, self.weight, self.bias, out)
+            return out[:, :self.n].clone()
         local = self.kernels.adaln_project(temb, self.weight, self.bias)   # [R, rows] fp32
         full = self.comm.all_gather_rows(local.contiguous())                # [R, world*rows]
         return full[:, :self.n]

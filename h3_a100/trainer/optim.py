@@ -64,7 +64,11 @@ class FlatAdamW:
         self.max_grad_norm = float(max_grad_norm)
         self.kernels, self.comm = kernels, comm
         world = comm.world_size if comm is not None else 1
-        self.shard = bool(shard_states) and world > 1
+        # The peer-memory transport runs the whole step (reduce-scatter, norm,
+        # clip, AdamW on the local shard, all-gather of the new parameters) in
+        # one kernel, so it always shards the optimizer state.
+        self.fused = world > 1 and hasattr(comm, "lora_step")
+        self.shard = (bool(shard_states) or self.fused) and world > 1
         param = store.flat
         n = param.numel()
         if self.shard:
@@ -96,6 +100,11 @@ class FlatAdamW:
         grad = self.store.ensure_grad()
         comm = self.comm
         k = self.kernels
+        if self.fused:
+            self.step_count += 1
+            comm.lora_step(self, lr)
+            self.last_grad_norm = comm.scratch[15:16]
+            return self.last_grad_norm
         if self.shard:
             full = grad if grad.numel() == self.padded else torch.nn.functional.pad(grad, (0, self.padded - grad.numel()))
             local = torch.empty(self.chunk, dtype=torch.float32, device=grad.device)

@@ -190,17 +190,35 @@ class H3DmdTrainer(CheckpointMixin, LoopMixin, DMDRuntimeMixin):
             offload_cpu_tensors=self.device.type == "cpu")
 
     # ---------------------------------------------------------------- setup
+    def _build_comm(self):
+        """NCCL baseline or the peer-memory kernels (``distributed.comm``), chosen once."""
+        from ..parallel.comm import TorchComm
+
+        kind = str(get(self.config, "distributed.comm", "nccl"))
+        world = pdist.get_world_size()
+        if kind == "p2p" and world > 1 and self.device.type == "cuda" and getattr(self.kernels, "native", False):
+            from ..parallel.p2p import PeerComm
+
+            if pdist.topology().replicate_size != 1:
+                raise ValueError("distributed.comm=p2p needs a single shard group (one NVLink domain)")
+            return PeerComm(pdist.shard_group(), self.device, kernels=self.kernels)
+        if kind not in {"nccl", "p2p"}:
+            raise ValueError(f"distributed.comm must be 'nccl' or 'p2p', got {kind!r}")
+        return TorchComm(pdist.shard_group(), self.device)
+
     def setup(self, resume_ckpt_path: str | None = None, *, comm=None) -> None:
         model = self.model
+        self.comm = comm or self._build_comm()
+        pad = 4 * max(1, self.comm.world_size)
         model.prepare_shared_backbone(student_lora=self.student_lora_config, fake_lora=self.fake_lora_config,
                                       cache_enabled=self.adaln_cache_enabled,
-                                      max_dynamic_cache_keys=self.adaln_dynamic_keys)
+                                      max_dynamic_cache_keys=self.adaln_dynamic_keys,
+                                      alloc=self.comm.alloc_symmetric if self.comm.world_size > 1 else None,
+                                      pad_to=pad)
         dit = model.denoiser_module()
         self._validate_reorder_contract()
         if resume_ckpt_path is not None:
             self._load_role_weights_before_sharding(resume_ckpt_path)
-        from ..parallel.comm import TorchComm
-        self.comm = comm or TorchComm(pdist.shard_group(), self.device)
         reshard = get(self.config, "distributed.fsdp2.reshard_after_forward", {}) or {}
         fsdp_enabled = bool(get(self.config, "distributed.fsdp2.enabled", True))
         shard_comm = self.comm if fsdp_enabled else _LocalComm(self.device)

@@ -19,6 +19,7 @@ SOURCES = [
     "csrc/attn/attention_fwd.cu",
     "csrc/attn/attention_bwd.cu",
     "csrc/noalloc/dmd_loss_noalloc.cu",
+    "csrc/comm/p2p.cu",
     "csrc/staging/pinned_pool.cpp",
 ]
 NVCC_FLAGS = [

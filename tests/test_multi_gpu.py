@@ -1,0 +1,194 @@
+"""Peer-memory collectives on 2 GPUs, compared with NCCL + the PyTorch oracle.
+
+Runs as spawned ranks (one per GPU, NCCL over 127.0.0.1, short process-group
+timeout).  Skipped when fewer than two GPUs are visible.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+import traceback
+from datetime import timedelta
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+WORLD = 2
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _init(rank: int, port: int) -> torch.device:
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(WORLD),
+                      LOCAL_RANK=str(rank))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    return dev
+
+
+def _collectives(rank: int, port: int, errors) -> None:
+    try:
+        dev = _init(rank, port)
+        from h3_a100.ops.native import NativeKernels
+        from h3_a100.ops.torch_kernels import TorchKernels
+        from h3_a100.parallel.p2p import PeerComm
+
+        K = NativeKernels(dev)
+        comm = PeerComm(None, dev, kernels=K)
+        # 1. pull all-gather of a symmetric shard
+        shard = comm.alloc_shard(4096, torch.bfloat16)
+        shard.copy_(torch.arange(4096, device=dev, dtype=torch.float32).to(torch.bfloat16) + 1000 * rank)
+        dist.barrier()
+        pending = comm.all_gather_async(shard, 4096 * WORLD)
+        full = comm.wait(pending)
+        ref = torch.empty(4096 * WORLD, dtype=torch.bfloat16, device=dev)
+        dist.all_gather_into_tensor(ref, shard)
+        torch.cuda.synchronize()
+        assert torch.equal(full, ref), "p2p all-gather != NCCL all-gather"
+        # 2. AdaLN GEMV with fused output all-gather
+        g = torch.Generator(device=dev).manual_seed(0)
+        temb = torch.randn(2, 512, device=dev, generator=g).to(torch.bfloat16)
+        w_full = (torch.randn(6 * 128, 512, device=dev, generator=g) * 0.05).to(torch.bfloat16)
+        b_full = torch.randn(6 * 128, device=dev, generator=g).to(torch.bfloat16)
+        rows = w_full.shape[0] // WORLD
+        out = comm.alloc_symmetric(2 * WORLD * rows, torch.float32)[: 2 * WORLD * rows].view(2, -1)
+        comm.adaln_project(temb, w_full[rank * rows:(rank + 1) * rows].contiguous(),
+                           b_full[rank * rows:(rank + 1) * rows].contiguous(), out)
+        torch.cuda.synchronize()
+        comm.check_status()
+        ref = TorchKernels().adaln_project(temb.float(), w_full.float(), b_full.float())
+        err = (out - ref).abs().max().item()
+        assert err < 1e-2 * ref.abs().max().item(), f"adaln gather error {err}"
+        # 3. fused LoRA reduce-scatter + clip + AdamW + all-gather vs NCCL + reference AdamW
+        from h3_a100.trainer.optim import FlatAdamW
+
+        class Store:
+            def __init__(self, flat, grad):
+                self.flat, self.grad = flat, grad
+
+            def ensure_grad(self):
+                return self.grad
+
+            def zero_grad(self):
+                self.grad.zero_()
+
+        n = 8192
+        flat = comm.alloc_symmetric(n, torch.bfloat16)
+        grad = comm.alloc_symmetric(n, torch.float32)
+        init = torch.randn(n, device=dev, generator=torch.Generator(device=dev).manual_seed(1))
+        flat.copy_(init.to(torch.bfloat16))
+        opt = FlatAdamW(Store(flat, grad), lr=1e-2, weight_decay=0.01, max_grad_norm=1.0, kernels=K, comm=comm)
+        assert opt.fused and opt.shard
+        ref_store = Store(init.to(torch.bfloat16).clone(), torch.zeros(n, device=dev))
+        ref_opt = FlatAdamW(ref_store, lr=1e-2, weight_decay=0.01, max_grad_norm=1.0, kernels=TorchKernels(),
+                            comm=None)
+        for step in range(2):
+            gen = torch.Generator(device=dev).manual_seed(10 + step + 100 * rank)
+            local_grad = torch.randn(n, device=dev, generator=gen) * (step + 1)
+            grad.copy_(local_grad)
+            dist.barrier()
+            opt.step(1e-2)
+            torch.cuda.synchronize()
+            comm.check_status()
+            avg = local_grad.clone()
+            dist.all_reduce(avg)
+            ref_store.grad.copy_(avg / WORLD)
+            ref_opt.step(1e-2)
+            err = (flat.float() - ref_store.flat.float()).abs().max().item()
+            assert err < 2e-2, f"fused LoRA step mismatch {err} at step {step}"
+        dist.barrier()
+    except Exception:  # noqa: BLE001 - reported to the parent
+        errors.put(f"rank {rank}: {traceback.format_exc()}")
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def _cycle(rank: int, port: int, comm_kind: str, results, errors) -> None:
+    try:
+        _init(rank, port)
+        os.environ["H3_EXPECTED_WORLD_SIZE"] = str(WORLD)
+        from h3_a100.api import build_trainer
+        from h3_a100.config import load_config
+
+        root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+        config = load_config(os.path.join(root, "configs", "h3_dmd_smoke_gpu.yaml"),
+                             {"distributed": {"comm": comm_kind, "timeout_minutes": 2},
+                              "training": {"max_train_iters": 2}})
+        trainer = build_trainer(config)
+        trainer.setup()
+        samples = trainer.samples()
+        losses = [trainer.run_cycle(samples, i) for i in range(2)]
+        torch.cuda.synchronize()
+        trainer.kernels.check_status()
+        if rank == 0:
+            results.put((comm_kind, losses, trainer.model.lora["student"].flat.float().sum().item()))
+        trainer.data.close()
+    except Exception:  # noqa: BLE001
+        errors.put(f"rank {rank} ({comm_kind}): {traceback.format_exc()}")
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def _spawn(fn, port):
+    ctx = mp.get_context("spawn")
+    errors = ctx.Queue()
+    procs = [ctx.Process(target=fn, args=(r, port, errors)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=600)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    msgs = []
+    while not errors.empty():
+        msgs.append(errors.get())
+    return msgs, [p.exitcode for p in procs]
+
+
+@pytest.fixture(scope="module")
+def two_gpus():
+    if not torch.cuda.is_available() or torch.cuda.device_count() < WORLD:
+        pytest.skip("needs two GPUs")
+
+
+def test_peer_collectives_match_nccl(two_gpus):
+    msgs, codes = _spawn(_collectives, _free_port())
+    assert not msgs, "\n".join(msgs)
+    assert codes == [0] * WORLD
+
+
+def test_dmd_cycle_p2p_matches_nccl(two_gpus):
+    ctx = mp.get_context("spawn")
+    out = {}
+    for kind in ("nccl", "p2p"):
+        results = ctx.Queue()
+        port = _free_port()
+        errors = ctx.Queue()
+        procs = [ctx.Process(target=_cycle, args=(r, port, kind, results, errors)) for r in range(WORLD)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(timeout=900)
+        msgs = []
+        while not errors.empty():
+            msgs.append(errors.get())
+        assert not msgs, "\n".join(msgs)
+        out[kind] = results.get(timeout=5)
+    (_, l_nccl, s_nccl), (_, l_p2p, s_p2p) = out["nccl"], out["p2p"]
+    for a, b in zip(l_nccl, l_p2p):
+        assert abs(a["fake"] - b["fake"]) <= 2e-2 * max(1.0, abs(a["fake"])), (l_nccl, l_p2p)
+        assert abs(a["dmd"] - b["dmd"]) <= 5e-2 * max(1e-3, abs(a["dmd"])) + 1e-6, (l_nccl, l_p2p)
+    assert abs(s_nccl - s_p2p) <= 1e-2 * max(1.0, abs(s_nccl)), (s_nccl, s_p2p)
