@@ -104,7 +104,9 @@ def main() -> None:
     samples = trainer.samples()
 
     for w in range(args.warmup):
-        trainer.run_cycle(samples, w)
+        losses = trainer.run_cycle(samples, w)
+        if rank == 0:
+            print(f"warmup cycle {w}: losses {losses}", file=sys.stderr, flush=True)
     torch.cuda.synchronize()
     pdist.barrier()
     torch.cuda.synchronize()

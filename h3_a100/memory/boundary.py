@@ -79,11 +79,51 @@ def _pinned_empty(numel: int, dtype: torch.dtype) -> torch.Tensor:
     return _C.pinned_empty(numel, dtype)
 
 
-class PinnedSlabPool:
-    """Reusable host buffers keyed by (bytes, dtype); pinned when requested."""
+def host_available_bytes() -> int:
+    """MemAvailable from /proc/meminfo (0 when unreadable)."""
+    try:
+        with open("/proc/meminfo") as fh:
+            for line in fh:
+                if line.startswith("MemAvailable:"):
+                    return int(line.split()[1]) * 1024
+    except OSError:
+        pass
+    return 0
 
-    def __init__(self, pin_memory: bool) -> None:
-        self.pin_memory = bool(pin_memory) and torch.cuda.is_available()
+
+def choose_staging_target(requested: str, bytes_per_rank: int, local_ranks: int, device: torch.device) -> str:
+    """Resolve ``auto`` to ``host`` or ``device``.
+
+    ``host`` is the reference's policy (pinned host slabs).  ``device`` keeps
+    the slabs in HBM: the same copies and counters, but the boundaries never
+    leave the GPU.  ``auto`` picks ``host`` while every local rank's slabs fit
+    in half of the node's available RAM, else ``device`` (an 8-rank node with
+    20 GB of boundaries per rank would otherwise pin most of host memory).
+    """
+    requested = str(requested)
+    if requested not in {"auto", "host", "device"}:
+        raise ValueError(f"boundary staging target must be auto|host|device, got {requested!r}")
+    if requested != "auto":
+        return requested
+    if device.type != "cuda":
+        return "host"
+    avail = host_available_bytes()
+    return "host" if avail and bytes_per_rank * local_ranks <= avail // 2 else "device"
+
+
+class PinnedSlabPool:
+    """Reusable staging buffers keyed by (bytes, dtype).
+
+    ``target="host"``: host slabs, pinned when requested.  ``target="device"``:
+    slabs in the GPU's own memory (``device`` must then be a CUDA device).
+    """
+
+    def __init__(self, pin_memory: bool, target: str = "host", device: torch.device | None = None) -> None:
+        self.target = str(target)
+        self.device = device
+        if self.target == "device" and (device is None or device.type != "cuda"):
+            raise ValueError("device staging needs a CUDA device")
+        self.pin_memory = bool(pin_memory) and torch.cuda.is_available() and self.target == "host"
         self._free: dict[tuple[int, torch.dtype], list[torch.Tensor]] = defaultdict(list)
         self.allocated_bytes = 0
         self._pending: list[tuple[torch.Tensor, Any]] = []
@@ -104,7 +144,12 @@ class PinnedSlabPool:
             self._sweep()
             if self._free[key]:
                 return self._free[key].pop()
-        slab = _pinned_empty(int(numel), dtype) if self.pin_memory else torch.empty(int(numel), dtype=dtype)
+        if self.target == "device":
+            slab = torch.empty(int(numel), dtype=dtype, device=self.device)
+        elif self.pin_memory:
+            slab = _pinned_empty(int(numel), dtype)
+        else:
+            slab = torch.empty(int(numel), dtype=dtype)
         self.allocated_bytes += slab.numel() * slab.element_size()
         return slab
 
@@ -184,19 +229,25 @@ class BoundaryStager:
         if stream is None:
             staged.upload = staged.slab.clone()
             return
-        staged.upload = torch.empty(staged.slab.numel(), dtype=staged.dtype, device=staged.device)
         with torch.cuda.stream(stream):
+            # Allocate from the copy stream's pool.  A block taken from the
+            # compute stream's pool may have been freed by kernels that are
+            # still queued there; writing it from this stream without waiting
+            # for them would corrupt their data.  The consumer stream is
+            # recorded on the tensor when it is handed out (stage_in).
+            staged.upload = torch.empty(staged.slab.numel(), dtype=staged.dtype, device=staged.device)
             if staged.d2h_done is not None:
                 stream.wait_event(staged.d2h_done)
             staged.upload.copy_(staged.slab, non_blocking=True)
             staged.h2d_done = torch.cuda.Event()
             staged.h2d_done.record(stream)
-        staged.upload.record_stream(stream)
 
     def stage_in(self, staged: _Staged) -> torch.Tensor:
         self._start_upload(staged)
         if staged.h2d_done is not None:
-            torch.cuda.current_stream(staged.device).wait_event(staged.h2d_done)
+            consumer = torch.cuda.current_stream(staged.device)
+            consumer.wait_event(staged.h2d_done)
+            staged.upload.record_stream(consumer)
         out = torch.as_strided(staged.upload, staged.shape, staged.stride)
         index = next((i for i, item in enumerate(self._stack) if item is staged), None)
         if index is not None:

@@ -48,6 +48,16 @@ def dit_config_from(config: dict[str, Any]) -> DiTConfig:
     return DiTConfig.from_dict(model)
 
 
+def sequence_tokens(config: dict[str, Any]) -> int:
+    """Joint sequence length: patchified video + text + audio tokens."""
+    dit = dit_config_from(config)
+    v = get(config, "synthetic.video_latent_shape", [0, 0, 0, 0])
+    tokens = (v[1] // dit.patch[0]) * (v[2] // dit.patch[1]) * (v[3] // dit.patch[2])
+    tokens += int((get(config, "synthetic.text_shape") or [0])[0])
+    tokens += int((get(config, "synthetic.audio_latent_shape") or [0, 0])[1])
+    return tokens
+
+
 class H3SharedBackbone:
     def __init__(self, config: dict[str, Any], *, device: torch.device, kernels, comm=None) -> None:
         self.config = config

@@ -76,22 +76,20 @@ def run(config_path: str | None = None) -> dict:
     c["host_ram_gib"] = round(ram, 1)
     if config_path:
         from .config import load_config
-        from .models.shared_backbone import dit_config_from
+        from .models.shared_backbone import dit_config_from, sequence_tokens
 
         cfg = load_config(config_path)
         dit = dit_config_from(cfg)
-        syn = cfg.get("synthetic", {})
-        vshape = syn.get("video_latent_shape", [0, 0, 0, 0])
-        tokens = (vshape[1] // dit.patch[0]) * (vshape[2] // dit.patch[1]) * (vshape[3] // dit.patch[2])
-        tokens += int(syn.get("text_shape", [0])[0]) + int((syn.get("audio_latent_shape") or [0, 0])[1])
+        tokens = sequence_tokens(cfg)
         boundary = tokens * dit.hidden * 2
         ranks = int(os.environ.get("LOCAL_WORLD_SIZE", max(1, torch.cuda.device_count())))
         pinned = boundary * dit.num_blocks * ranks / 1024**3
         c["config"] = {"path": config_path, "tokens": tokens, "boundary_bytes": boundary,
                        "frozen_params": dit.param_counts()["frozen_total"],
                        "pinned_boundary_gib_per_node": round(pinned, 1)}
-        if ram and pinned > 0.9 * ram:
-            report["errors"].append(f"boundary staging pins {pinned:.0f} GiB on this node but host RAM is {ram:.0f} GiB")
+        if ram and pinned > 0.5 * ram:
+            report["warnings"].append(f"host boundary slabs would need {pinned:.0f} GiB of {ram:.0f} GiB RAM: "
+                                      "staging_target auto keeps them in HBM instead")
     report["ok"] = not report["errors"]
     return report
 

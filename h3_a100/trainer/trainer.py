@@ -21,7 +21,7 @@ import torch
 
 from ..config import env_flag, get, training_system_section
 from ..memory.boundary import POLICY_NAME as CHECKPOINT_BOUNDARY_CPU
-from ..memory.boundary import PinnedSlabPool, install_checkpoint_boundary_cpu_offload
+from ..memory.boundary import PinnedSlabPool, choose_staging_target, install_checkpoint_boundary_cpu_offload
 from ..memory.exact_replay import install_exact_adaln_checkpoint_replay_scope
 from ..memory.saved_tensor_offload import maybe_saved_tensor_offload
 from ..models.lora import FAKE, STUDENT
@@ -116,6 +116,8 @@ class H3DmdTrainer(CheckpointMixin, LoopMixin, DMDRuntimeMixin):
                              f"got {self.activation_policy!r}")
         self.boundary_offload_pin_memory = env_flag("H3_BOUNDARY_OFFLOAD_PIN_MEMORY", policy.get("pin_memory", True))
         self.boundary_offload_events = env_flag("H3_BOUNDARY_OFFLOAD_EVENTS", policy.get("detailed_events", False))
+        self.boundary_staging_target = str(os.environ.get("H3_BOUNDARY_STAGING_TARGET",
+                                                          policy.get("staging_target", "host")))
         self.activation_offload_enabled = env_flag("H3_ACTIVATION_OFFLOAD", False)
         self.activation_offload_min_bytes = int(os.environ.get("H3_ACTIVATION_OFFLOAD_MIN_BYTES", 128 * 1024 * 1024))
         self.activation_offload_pin_memory = env_flag("H3_ACTIVATION_OFFLOAD_PIN_MEMORY", True)
@@ -233,7 +235,12 @@ class H3DmdTrainer(CheckpointMixin, LoopMixin, DMDRuntimeMixin):
             event_path = None
             if self.boundary_offload_events:
                 event_path = Path(self.output_train_dir) / "checkpoint_boundary_offload" / f"rank_{pdist.get_rank():03d}.jsonl"
-            self.boundary_pool = PinnedSlabPool(self.boundary_offload_pin_memory)
+            per_rank = self._boundary_bytes_per_rank(model)
+            local_ranks = int(os.environ.get("LOCAL_WORLD_SIZE", "1"))
+            self.boundary_staging_target = choose_staging_target(
+                self.boundary_staging_target, per_rank, local_ranks, self.device)
+            self.boundary_pool = PinnedSlabPool(self.boundary_offload_pin_memory, self.boundary_staging_target,
+                                                self.device)
             self.boundary_offload_registration = install_checkpoint_boundary_cpu_offload(
                 dit, role_getter=model.current_role, event_path=event_path,
                 pin_memory=self.boundary_offload_pin_memory,
@@ -266,9 +273,17 @@ class H3DmdTrainer(CheckpointMixin, LoopMixin, DMDRuntimeMixin):
                     "sharded={} critic_reorder={} matched_compute={} kernels={}",
                     model.lora[STUDENT].numel(), model.lora[FAKE].numel(), model.is_sharded(),
                     self.reorder_critic_rollouts, self.matched_compute_enabled, self.kernels.name)
-        logger.info("[h3-a100] activation policy={} checkpoint_segment={} boundary_pin={} boundary_events={} "
-                    "legacy_threshold_offload={}", self.activation_policy, self.activation_checkpoint_segment_size,
-                    self.boundary_offload_pin_memory, self.boundary_offload_events, self.activation_offload_enabled)
+        logger.info("[h3-a100] activation policy={} checkpoint_segment={} boundary_pin={} boundary_target={} "
+                    "boundary_events={} legacy_threshold_offload={}", self.activation_policy,
+                    self.activation_checkpoint_segment_size, self.boundary_offload_pin_memory,
+                    self.boundary_staging_target, self.boundary_offload_events, self.activation_offload_enabled)
+
+    def _boundary_bytes_per_rank(self, model) -> int:
+        """Bytes of one grad forward's boundaries (one bf16 hidden state per block)."""
+        from ..models.shared_backbone import sequence_tokens
+
+        cfg = model.dit_config
+        return sequence_tokens(self.config) * cfg.hidden * 2 * cfg.num_blocks
 
     def reserve_boundary_slabs(self, per_forward: int, numel: int, dtype: torch.dtype) -> None:
         """Allocate the pinned boundary pool up front (one grad forward's worth)."""
