@@ -15,11 +15,12 @@
 //               issue order S_0 S_1 | PV_0 S_0' PV_1 S_1' | ..., so the tensor
 //               core works on one query tile while the other tile's softmax runs.
 //   warps 2..5  softmax of query tile 0, warps 6..9 of query tile 1; one query
-//               row per thread.  Pass 1 streams S_t from TMEM for the row max;
-//               pass 2 streams it again, computes 2^(s - m), accumulates the
-//               row sum and writes P as packed bf16 pairs back into the first
-//               64 TMEM columns of S_t (already consumed), where the PV MMA
-//               reads it.  O_t is rescaled in TMEM only when some row's max
+//               row per thread.  The row of S_t is read from TMEM once into
+//               128 registers; the row max and the row sum each run as eight
+//               independent chains (a single accumulator is a 128-deep
+//               dependency chain that dominated the softmax time); P = 2^(s - m)
+//               is written as packed bf16 pairs back into the first 64 TMEM
+//               columns of S_t, where the PV MMA reads it.  O_t is rescaled in TMEM only when some row's max
 //               grew by more than 2^8 (warp-uniform decision: tcgen05.ld/st
 //               are warp-collective).
 // TMEM: S_0 [0,128) S_1 [128,256) O_0 [256,384) O_1 [384,512) fp32 columns.
@@ -94,54 +95,68 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr));
 }
 
-// Row max of one 128-key S tile streamed from TMEM (raw scores; masked past `valid`).
-template <bool MASKED>
-__device__ __forceinline__ float row_max(uint32_t tS, int valid) {
-  uint32_t r[kBKV / 32][32];
+// One 128-key S row of this thread, loaded from TMEM once (four loads, one wait).
+__device__ __forceinline__ void load_row(uint32_t tS, uint32_t (&r)[kBKV / 32][32]) {
 #pragma unroll
-  for (int c = 0; c < kBKV / 32; ++c) tmem_ld32(tS + c * 32, r[c]);  // all loads in flight, one wait
+  for (int c = 0; c < kBKV / 32; ++c) tmem_ld32(tS + c * 32, r[c]);
   tmem_ld_wait();
-  float m = -INFINITY;
+}
+
+// Keys at or past `valid` get -inf (last KV tile only).
+__device__ __forceinline__ void mask_row(uint32_t (&r)[kBKV / 32][32], int valid) {
 #pragma unroll
   for (int c = 0; c < kBKV / 32; ++c)
 #pragma unroll
-    for (int i = 0; i < 32; ++i) m = fmaxf(m, (!MASKED || c * 32 + i < valid) ? __uint_as_float(r[c][i]) : -INFINITY);
-  return m;
+    for (int i = 0; i < 32; ++i)
+      if (c * 32 + i >= valid) r[c][i] = __float_as_uint(-INFINITY);
 }
 
-// Writes P = 2^(s*scale - m) as packed bf16 pairs over the consumed S columns; returns the row sum.
+// Row max with eight independent chains (a single running max would be a
+// 128-deep dependency chain on the critical path of every KV tile).
+__device__ __forceinline__ float row_max(const uint32_t (&r)[kBKV / 32][32]) {
+  float m[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) m[k] = __uint_as_float(r[0][k]);
+#pragma unroll
+  for (int c = 0; c < kBKV / 32; ++c)
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (c > 0 || i >= 8) m[i & 7] = fmaxf(m[i & 7], __uint_as_float(r[c][i]));
+  const float a = fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
+  const float b = fmaxf(fmaxf(m[4], m[5]), fmaxf(m[6], m[7]));
+  return fmaxf(a, b);
+}
+
+// P = 2^(s*scale - m) from the registers, stored as packed bf16 pairs over the
+// first 64 S columns; returns the row sum (four independent partial sums).
 template <bool MASKED>
-__device__ __forceinline__ float row_exp_pack(uint32_t tS, int valid, float scale, float m) {
-  float sum = 0.f;
+__device__ __forceinline__ float row_exp_pack(uint32_t tS, const uint32_t (&r)[kBKV / 32][32], int valid, float scale,
+                                              float m) {
+  float acc[4];
 #pragma unroll
-  for (int cp = 0; cp < kBKV / 64; ++cp) {
-    uint32_t r[2][32];
-    tmem_ld32(tS + cp * 64, r[0]);  // two chunks in flight per wait
-    tmem_ld32(tS + cp * 64 + 32, r[1]);
-    tmem_ld_wait();
+  for (int k = 0; k < 4; ++k) acc[k] = 0.f;
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int c = cp * 2 + h;
-      uint32_t packed[16];
+  for (int c = 0; c < kBKV / 32; ++c) {
+    uint32_t packed[16];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float xa = fmaf(__uint_as_float(r[h][2 * i]), scale, -m);
-        const float xb = fmaf(__uint_as_float(r[h][2 * i + 1]), scale, -m);
-        // one pair in four goes through the FMA-pipe exponential
-        float a = (i & 3) == 3 ? exp2_fma(xa) : ex2(xa);
-        float b = (i & 3) == 3 ? exp2_fma(xb) : ex2(xb);
-        if (MASKED) {
-          const int k0 = c * 32 + 2 * i;
-          a = k0 < valid ? a : 0.f;
-          b = k0 + 1 < valid ? b : 0.f;
-        }
-        sum += a + b;
-        packed[i] = pack_bf16x2(a, b);
+    for (int i = 0; i < 16; ++i) {
+      const float xa = fmaf(__uint_as_float(r[c][2 * i]), scale, -m);
+      const float xb = fmaf(__uint_as_float(r[c][2 * i + 1]), scale, -m);
+      // one pair in four goes through the FMA-pipe exponential
+      float a = (i & 3) == 3 ? exp2_fma(xa) : ex2(xa);
+      float b = (i & 3) == 3 ? exp2_fma(xb) : ex2(xb);
+      if (MASKED) {
+        const int k0 = c * 32 + 2 * i;
+        a = k0 < valid ? a : 0.f;
+        b = k0 + 1 < valid ? b : 0.f;
       }
-      tmem_st16(tS + c * 16, packed);
+      acc[(2 * i) & 3] += a;
+      acc[(2 * i + 1) & 3] += b;
+      packed[i] = pack_bf16x2(a, b);
     }
+    tmem_st16(tS + c * 16, packed);
   }
-  return sum;
+  return (acc[0] + acc[1]) + (acc[2] + acc[3]);
 }
 
 __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_constant__ CUtensorMap tm, FwdParams p) {
@@ -304,11 +319,19 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         ok = false;
         break;
       }
+      // O_t may be rescaled once PV_t of the previous tile completed (the
+      // commit order already implies it: S_t(j) was issued after PV_t(j-1)).
+      if (j > 0 && !mbar_wait(&o_done[t], (j - 1) & 1, limit, abort_flag)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
       const int kv_valid = p.T - j * kBKV;
-      // pass 1: row max (raw scores; the scale is positive)
-      float m_tile = kv_valid >= kBKV ? row_max<false>(tS, kv_valid) : row_max<true>(tS, kv_valid);
-      m_tile *= p.scale_log2;
+      // One TMEM read of the row; the max uses raw scores (the scale is positive).
+      uint32_t r[kBKV / 32][32];
+      load_row(tS, r);
+      if (kv_valid < kBKV) mask_row(r, kv_valid);
+      const float m_tile = row_max(r) * p.scale_log2;
       const float m_new = fmaxf(m_used, m_tile);
       const bool need = (j == 0) || (m_new > m_used + kRescaleThreshold);
       const bool warp_need = __any_sync(0xffffffffu, need);
@@ -316,11 +339,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       if (need) {
         l *= alpha;
         m_used = m_new;
-      }
-      // O_t and the P slot are free once PV_t of the previous tile completed.
-      if (j > 0 && !mbar_wait(&o_done[t], (j - 1) & 1, limit, abort_flag)) {
-        ok = false;
-        break;
       }
       tc_fence_after();
       if (warp_need && j > 0) {
@@ -334,9 +352,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
           tmem_st16(tO + c * 16, r);
         }
       }
-      // pass 2: P = 2^(s*scale - m) as packed bf16 pairs over the consumed S columns.
-      const float rowsum = kv_valid >= kBKV ? row_exp_pack<false>(tS, kv_valid, p.scale_log2, m_used)
-                                            : row_exp_pack<true>(tS, kv_valid, p.scale_log2, m_used);
+      // P = 2^(s*scale - m) as packed bf16 pairs over the consumed S columns.
+      const float rowsum = kv_valid >= kBKV ? row_exp_pack<false>(tS, r, kv_valid, p.scale_log2, m_used)
+                                            : row_exp_pack<true>(tS, r, kv_valid, p.scale_log2, m_used);
       l += rowsum;
       tmem_st_wait();
       tc_fence_before();

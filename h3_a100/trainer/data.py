@@ -109,7 +109,11 @@ class PinnedLoader:
         return self._queue.get()
 
     def close(self) -> None:
+        """Stop the producer and join it (a daemon thread killed inside a torch
+        call at interpreter exit can abort the process)."""
         self._stop.set()
+        if self._thread.is_alive() and self._thread is not threading.current_thread():
+            self._thread.join(timeout=30)
 
 
 def to_device(sample: dict[str, Any], device: torch.device) -> dict[str, Any]:
