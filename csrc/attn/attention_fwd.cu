@@ -27,6 +27,7 @@
 // Keys past T are masked to -inf; queries past T are computed and not stored.
 // Every wait is bounded (see ptx.cuh).  Every TMA load targets one CTA only.
 #include <ATen/cuda/CUDAContext.h>
+#include <cstdlib>
 #include <c10/cuda/CUDAGuard.h>
 #include <cudaTypedefs.h>
 #include <torch/extension.h>
@@ -95,6 +96,33 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr));
 }
 
+// Three-input max (sm_100 PTX): halves the max instructions per element.
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Packed f32x2 arithmetic (sm_100): one instruction for two lanes of a pair.
+__device__ __forceinline__ uint64_t pack2(float a, float b) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(a), "f"(b));
+  return d;
+}
+__device__ __forceinline__ void unpack2(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 // One 128-key S row of this thread, loaded from TMEM once (four loads, one wait).
 __device__ __forceinline__ void load_row(uint32_t tS, uint32_t (&r)[kBKV / 32][32]) {
 #pragma unroll
@@ -111,54 +139,59 @@ __device__ __forceinline__ void mask_row(uint32_t (&r)[kBKV / 32][32], int valid
       if (c * 32 + i >= valid) r[c][i] = __float_as_uint(-INFINITY);
 }
 
-// Row max with eight independent chains (a single running max would be a
-// 128-deep dependency chain on the critical path of every KV tile).
+// Row max: eight independent chains of three-input maxes (a single running
+// max is a 128-deep dependency chain on the critical path of every KV tile).
 __device__ __forceinline__ float row_max(const uint32_t (&r)[kBKV / 32][32]) {
   float m[8];
 #pragma unroll
-  for (int k = 0; k < 8; ++k) m[k] = __uint_as_float(r[0][k]);
+  for (int k = 0; k < 8; ++k) m[k] = fmaxf(__uint_as_float(r[0][2 * k]), __uint_as_float(r[0][2 * k + 1]));
 #pragma unroll
   for (int c = 0; c < kBKV / 32; ++c)
 #pragma unroll
-    for (int i = 0; i < 32; ++i)
-      if (c > 0 || i >= 8) m[i & 7] = fmaxf(m[i & 7], __uint_as_float(r[c][i]));
-  const float a = fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
-  const float b = fmaxf(fmaxf(m[4], m[5]), fmaxf(m[6], m[7]));
-  return fmaxf(a, b);
+    for (int i = 0; i < 16; ++i)
+      if (c > 0 || i >= 8)
+        m[i & 7] = fmax3(m[i & 7], __uint_as_float(r[c][2 * i]), __uint_as_float(r[c][2 * i + 1]));
+  return fmaxf(fmax3(m[0], m[1], m[2]), fmax3(fmax3(m[3], m[4], m[5]), m[6], m[7]));
 }
 
 // P = 2^(s*scale - m) from the registers, stored as packed bf16 pairs over the
-// first 64 S columns; returns the row sum (four independent partial sums).
-template <bool MASKED>
+// first 64 S columns; returns the row sum.  The scale/offset and the sum use
+// packed f32x2 instructions (four independent pair accumulators).  POLY > 0
+// sends one pair in POLY through the FMA-pipe exponential, the rest to MUFU.
+template <bool MASKED, int POLY>
 __device__ __forceinline__ float row_exp_pack(uint32_t tS, const uint32_t (&r)[kBKV / 32][32], int valid, float scale,
                                               float m) {
-  float acc[4];
+  const uint64_t scale2 = pack2(scale, scale), negm2 = pack2(-m, -m);
+  uint64_t acc[4];
 #pragma unroll
-  for (int k = 0; k < 4; ++k) acc[k] = 0.f;
+  for (int k = 0; k < 4; ++k) acc[k] = 0ull;   // (0.f, 0.f)
 #pragma unroll
   for (int c = 0; c < kBKV / 32; ++c) {
     uint32_t packed[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-      const float xa = fmaf(__uint_as_float(r[c][2 * i]), scale, -m);
-      const float xb = fmaf(__uint_as_float(r[c][2 * i + 1]), scale, -m);
-      // one pair in four goes through the FMA-pipe exponential
-      float a = (i & 3) == 3 ? exp2_fma(xa) : ex2(xa);
-      float b = (i & 3) == 3 ? exp2_fma(xb) : ex2(xb);
+      float xa, xb;
+      unpack2(fma2(pack2(__uint_as_float(r[c][2 * i]), __uint_as_float(r[c][2 * i + 1])), scale2, negm2), xa, xb);
+      const bool poly = POLY > 0 && (i % (POLY > 0 ? POLY : 1)) == (POLY > 0 ? POLY - 1 : 0);
+      float a = poly ? exp2_fma(xa) : ex2(xa);
+      float b = poly ? exp2_fma(xb) : ex2(xb);
       if (MASKED) {
         const int k0 = c * 32 + 2 * i;
         a = k0 < valid ? a : 0.f;
         b = k0 + 1 < valid ? b : 0.f;
       }
-      acc[(2 * i) & 3] += a;
-      acc[(2 * i + 1) & 3] += b;
+      acc[i & 3] = add2(acc[i & 3], pack2(a, b));
       packed[i] = pack_bf16x2(a, b);
     }
     tmem_st16(tS + c * 16, packed);
   }
-  return (acc[0] + acc[1]) + (acc[2] + acc[3]);
+  const uint64_t s2 = add2(add2(acc[0], acc[1]), add2(acc[2], acc[3]));
+  float sa, sb;
+  unpack2(s2, sa, sb);
+  return sa + sb;
 }
 
+template <int POLY>
 __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_constant__ CUtensorMap tm, FwdParams p) {
   constexpr uint32_t kIdescS = umma_idesc_bf16(kBQ, kBKV, false, false);
   constexpr uint32_t kIdescPV = umma_idesc_bf16(kBQ, kD, false, true);
@@ -341,21 +374,24 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         m_used = m_new;
       }
       tc_fence_after();
+      // P = 2^(s*scale - m) as packed bf16 pairs over the consumed S columns.
+      const float rowsum = kv_valid >= kBKV ? row_exp_pack<false, POLY>(tS, r, kv_valid, p.scale_log2, m_used)
+                                            : row_exp_pack<true, POLY>(tS, r, kv_valid, p.scale_log2, m_used);
+      l += rowsum;
+      // Rescale O_t after P is written (the S registers are dead by then, so
+      // the O chunk does not push the row past the register budget); PV_t(j)
+      // is issued only after p_full, i.e. after this.
       if (warp_need && j > 0) {
 #pragma unroll
         for (int c = 0; c < kD / 16; ++c) {
-          uint32_t r[16];
-          tmem_ld16(tO + c * 16, r);
+          uint32_t o[16];
+          tmem_ld16(tO + c * 16, o);
           tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-          tmem_st16(tO + c * 16, r);
+          for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st16(tO + c * 16, o);
         }
       }
-      // P = 2^(s*scale - m) as packed bf16 pairs over the consumed S columns.
-      const float rowsum = kv_valid >= kBKV ? row_exp_pack<false>(tS, r, kv_valid, p.scale_log2, m_used)
-                                            : row_exp_pack<true>(tS, r, kv_valid, p.scale_log2, m_used);
-      l += rowsum;
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&p_full[t]);
@@ -426,11 +462,21 @@ std::vector<at::Tensor> attention_fwd(const at::Tensor& qkv, int64_t heads, int6
   static bool configured[64] = {false};
   const int device = qkv.get_device();
   if (!configured[device]) {
-    cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    cudaFuncSetAttribute(attn_fwd_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    cudaFuncSetAttribute(attn_fwd_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
     configured[device] = true;
   }
+  // Exponential split: 0 = all on MUFU (default), 4 = one pair in four on the
+  // FMA pipe.  H3_ATTN_FWD_POLY selects it for measurements only.
+  static const int poly = [] {
+    const char* v = std::getenv("H3_ATTN_FWD_POLY");
+    return v != nullptr ? std::atoi(v) : 0;
+  }();
   dim3 grid(static_cast<unsigned>((T + kQTiles * kBQ - 1) / (kQTiles * kBQ)), static_cast<unsigned>(heads));
-  attn_fwd_kernel<<<grid, kThreads, kSmem, at::cuda::getCurrentCUDAStream(device).stream()>>>(tm, p);
+  if (poly == 4)
+    attn_fwd_kernel<4><<<grid, kThreads, kSmem, at::cuda::getCurrentCUDAStream(device).stream()>>>(tm, p);
+  else
+    attn_fwd_kernel<0><<<grid, kThreads, kSmem, at::cuda::getCurrentCUDAStream(device).stream()>>>(tm, p);
   note_launch();
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {o, lse};

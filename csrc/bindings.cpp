@@ -20,6 +20,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("lora_rs_adamw", &h3::lora_rs_adamw, "fused LoRA reduce-scatter + clip + AdamW + all-gather");
   m.def("adaln_project_gather", &h3::adaln_project_gather, "row-sharded AdaLN GEMV with fused output all-gather");
   m.def("wait_flag_test", &h3::wait_flag_test, "bounded wait on a flag (failure-detection tests)");
+  m.def("enable_peer_access", &h3::enable_peer_access, "let kernels on a device load from a peer GPU");
   m.def("launch_count", &h3::launch_count, "number of kernels launched by this extension");
   m.def("norm_modulate_fwd", &h3::norm_modulate_fwd);
   m.def("norm_modulate_bwd", &h3::norm_modulate_bwd);

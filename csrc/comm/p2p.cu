@@ -56,10 +56,11 @@ __device__ __forceinline__ void fence_sys() { asm volatile("fence.acq_rel.sys;" 
 __device__ bool wait_flag(const int* flag, int epoch, uint64_t limit_ns) {
   if (ld_acquire_sys(flag) - epoch >= 0) return true;
   const uint64_t start = global_timer_ns();
-  for (uint32_t it = 1;; ++it) {
+  for (uint32_t it = 1; it != 0u; ++it) {   // also bounded by the iteration count
     if (ld_acquire_sys(flag) - epoch >= 0) return true;
     if ((it & 255u) == 0u && global_timer_ns() - start > limit_ns) return false;
   }
+  return false;
 }
 
 // Signal slot layout: flags[slot * kMaxRanks + sender].
@@ -91,7 +92,7 @@ __device__ bool grid_barrier(int* bar, uint64_t limit_ns) {
     } else {
       const uint64_t start = global_timer_ns();
       for (uint32_t it = 1; *gen == g; ++it) {
-        if ((it & 255u) == 0u && global_timer_ns() - start > limit_ns) {
+        if (it == 0u || ((it & 255u) == 0u && global_timer_ns() - start > limit_ns)) {
           ok = false;
           break;
         }
@@ -430,12 +431,30 @@ void adaln_project_gather(const at::Tensor& temb, const at::Tensor& w, const c10
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// The wait runs on the device that holds `status`; `flag` may live on a peer
+// GPU (read with plain peer loads once peer access is enabled).
 void wait_flag_test(const at::Tensor& flag, int64_t epoch, const at::Tensor& status, int64_t limit_ns) {
-  c10::cuda::CUDAGuard guard(flag.get_device());
-  wait_flag_test_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream(flag.get_device()).stream()>>>(
+  TORCH_CHECK(flag.is_cuda() && status.is_cuda() && flag.scalar_type() == at::kInt && status.numel() >= 4,
+              "wait_flag_test operands");
+  c10::cuda::CUDAGuard guard(status.get_device());
+  wait_flag_test_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream(status.get_device()).stream()>>>(
       flag.data_ptr<int>(), static_cast<int>(epoch), status_of(status, limit_ns));
   note_launch();
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Lets kernels on `device` load from `peer`'s memory directly (idempotent).
+void enable_peer_access(int64_t device, int64_t peer) {
+  c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  int can = 0;
+  C10_CUDA_CHECK(cudaDeviceCanAccessPeer(&can, static_cast<int>(device), static_cast<int>(peer)));
+  TORCH_CHECK(can, "device ", device, " cannot access device ", peer, " directly");
+  const cudaError_t err = cudaDeviceEnablePeerAccess(static_cast<int>(peer), 0);
+  if (err == cudaErrorPeerAccessAlreadyEnabled) {
+    (void)cudaGetLastError();
+    return;
+  }
+  C10_CUDA_CHECK(err);
 }
 
 }  // namespace h3

@@ -16,5 +16,6 @@ void adaln_project_gather(const at::Tensor& temb, const at::Tensor& w, const c10
                           const std::vector<int64_t>& out_ptrs, const std::vector<int64_t>& flag_ptrs, int64_t rank,
                           int64_t epoch, int64_t slot, const at::Tensor& status, int64_t limit_ns);
 void wait_flag_test(const at::Tensor& flag, int64_t epoch, const at::Tensor& status, int64_t limit_ns);
+void enable_peer_access(int64_t device, int64_t peer);
 
 }  // namespace h3

@@ -85,13 +85,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64
                                           volatile int* abort) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = global_timer_ns();
-  for (uint32_t it = 1;; ++it) {
+  // The iteration count is a second bound, independent of the timer: the
+  // loop ends after 2^32 - 1 polls whatever %globaltimer reads.
+  for (uint32_t it = 1; it != 0u; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 63u) == 0u) {
       if (*abort) return false;
       if (global_timer_ns() - start > limit_ns) return false;
     }
   }
+  return false;
 }
 
 // ---------------------------------------------------------------- TMA
