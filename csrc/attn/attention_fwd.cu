@@ -45,7 +45,14 @@ constexpr int kBQ = 128;
 constexpr int kBKV = 128;
 constexpr int kD = 128;
 constexpr int kQTiles = 2;
-constexpr int kThreads = 64 + kQTiles * 128;
+constexpr int kThreads = 128 + kQTiles * 128;   // producer warpgroup + one softmax warpgroup per tile
+// Register split (setmaxnreg): launched at 168 per thread (384 x 168 = 64512),
+// the producer warpgroup drops to 72 and each softmax warpgroup rises to 216:
+// 128 x 72 + 256 x 216 = 64512, exactly the launch total (checked on the host).
+constexpr int kLaunchRegs = 168;
+constexpr int kRegsLow = 72;
+constexpr int kRegsHigh = 216;
+static_assert(128 * kRegsLow + kQTiles * 128 * kRegsHigh == kThreads * kLaunchRegs, "register split");
 constexpr int kChunk = 128 * 64 * 2;    // 128 rows x 64 bf16 (one 128B-swizzled column chunk)
 constexpr int kTileBytes = 2 * kChunk;  // 128 rows x 128 bf16
 constexpr int kSmem = 1024 + kTileBytes * (kQTiles + 4) + 512;  // Q x2, K[2], V[2]
@@ -94,6 +101,15 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
         "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
+}
+
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
 }
 
 // Three-input max (sm_100 PTX): halves the max instructions per element.
@@ -191,57 +207,14 @@ __device__ __forceinline__ float row_exp_pack(uint32_t tS, const uint32_t (&r)[k
   return sa + sb;
 }
 
-template <int POLY>
-__global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_constant__ CUtensorMap tm, FwdParams p) {
+// Producer warpgroup roles: warp 0 issues the TMA loads, warp 1 the MMAs.
+__device__ __forceinline__ void producer_warps(const CUtensorMap& tm, const FwdParams& p, int warp, uint8_t* sQ,
+                                               uint8_t* sK, uint8_t* sV, uint64_t* q_full, uint64_t* kv_full,
+                                               uint64_t* kv_empty, uint64_t* s_full, uint64_t* p_full,
+                                               uint64_t* o_done, uint64_t* drain, volatile int* abort_flag,
+                                               uint32_t tmem, int head, int q0, int n_kv, uint64_t limit) {
   constexpr uint32_t kIdescS = umma_idesc_bf16(kBQ, kBKV, false, false);
   constexpr uint32_t kIdescPV = umma_idesc_bf16(kBQ, kD, false, true);
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;                        // kQTiles tiles
-  uint8_t* sK = sQ + kQTiles * kTileBytes;   // 2 stages
-  uint8_t* sV = sK + 2 * kTileBytes;         // 2 stages
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + 2 * kTileBytes);
-  uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;   // [2]
-  uint64_t* kv_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;    // [kQTiles]
-  uint64_t* p_full = bars + 7;    // [kQTiles]
-  uint64_t* o_done = bars + 9;    // [kQTiles]
-  uint64_t* drain = bars + 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-
-  const int warp = warp_id(), lane = lane_id();
-  const int head = blockIdx.y;
-  const int q0 = blockIdx.x * (kQTiles * kBQ);
-  const int n_kv = p.n_kv;
-  const uint64_t limit = p.status.limit_ns;
-
-  if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
-    }
-    for (int t = 0; t < kQTiles; ++t) {
-      mbar_init(&s_full[t], 1);
-      mbar_init(&p_full[t], 128);
-      mbar_init(&o_done[t], 1);
-    }
-    mbar_init(drain, 1);
-    *abort_flag = 0;
-    fence_barrier_init();
-  }
-  if (warp == 0 && lane == 0) tma_prefetch_desc(&tm);
-  if (warp == 1) {
-    tmem_alloc(tmem_slot, 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (elect_one()) {
@@ -337,102 +310,167 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         mbar_wait(drain, 0, limit, &never);
       }
     }
-  } else {
-    // ------------------------------------------------------------ softmax (two warpgroups)
-    const int t = (warp - 2) >> 2;           // query tile handled by this warpgroup
-    const int quarter = warp & 3;            // TMEM lane quarter this warp may access
-    const int row = quarter * 32 + lane;
-    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t tS = tmem + t * 128 + lane_off;
-    const uint32_t tO = tmem + 256 + t * 128 + lane_off;
-    float m_used = -INFINITY, l = 0.f;
-    bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      if (!mbar_wait(&s_full[t], j & 1, limit, abort_flag)) {
-        ok = false;
-        break;
-      }
-      // O_t may be rescaled once PV_t of the previous tile completed (the
-      // commit order already implies it: S_t(j) was issued after PV_t(j-1)).
-      if (j > 0 && !mbar_wait(&o_done[t], (j - 1) & 1, limit, abort_flag)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const int kv_valid = p.T - j * kBKV;
-      // One TMEM read of the row; the max uses raw scores (the scale is positive).
-      uint32_t r[kBKV / 32][32];
-      load_row(tS, r);
-      if (kv_valid < kBKV) mask_row(r, kv_valid);
-      const float m_tile = row_max(r) * p.scale_log2;
-      const float m_new = fmaxf(m_used, m_tile);
-      const bool need = (j == 0) || (m_new > m_used + kRescaleThreshold);
-      const bool warp_need = __any_sync(0xffffffffu, need);
-      const float alpha = need ? ex2(m_used - m_new) : 1.f;
-      if (need) {
-        l *= alpha;
-        m_used = m_new;
-      }
-      tc_fence_after();
-      // P = 2^(s*scale - m) as packed bf16 pairs over the consumed S columns.
-      const float rowsum = kv_valid >= kBKV ? row_exp_pack<false, POLY>(tS, r, kv_valid, p.scale_log2, m_used)
-                                            : row_exp_pack<true, POLY>(tS, r, kv_valid, p.scale_log2, m_used);
-      l += rowsum;
-      // Rescale O_t after P is written (the S registers are dead by then, so
-      // the O chunk does not push the row past the register budget); PV_t(j)
-      // is issued only after p_full, i.e. after this.
-      if (warp_need && j > 0) {
-#pragma unroll
-        for (int c = 0; c < kD / 16; ++c) {
-          uint32_t o[16];
-          tmem_ld16(tO + c * 16, o);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st16(tO + c * 16, o);
-        }
-      }
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(&p_full[t]);
+  }
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+template <int POLY>
+__global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_constant__ CUtensorMap tm, FwdParams p) {
+  constexpr uint32_t kIdescS = umma_idesc_bf16(kBQ, kBKV, false, false);
+  constexpr uint32_t kIdescPV = umma_idesc_bf16(kBQ, kD, false, true);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;                        // kQTiles tiles
+  uint8_t* sK = sQ + kQTiles * kTileBytes;   // 2 stages
+  uint8_t* sV = sK + 2 * kTileBytes;         // 2 stages
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + 2 * kTileBytes);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;    // [kQTiles]
+  uint64_t* p_full = bars + 7;    // [kQTiles]
+  uint64_t* o_done = bars + 9;    // [kQTiles]
+  uint64_t* drain = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = warp_id(), lane = lane_id();
+  const int head = blockIdx.y;
+  const int q0 = blockIdx.x * (kQTiles * kBQ);
+  const int n_kv = p.n_kv;
+  const uint64_t limit = p.status.limit_ns;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
     }
-    const int q = q0 + t * kBQ + row;
-    if (ok && n_kv > 0 && mbar_wait(&o_done[t], (n_kv - 1) & 1, limit, abort_flag)) {
+    for (int t = 0; t < kQTiles; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 128);
+      mbar_init(&o_done[t], 1);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) tma_prefetch_desc(&tm);
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (warp < 4) {
+    // Producer warpgroup: warp 0 TMA, warp 1 MMA issuer, warps 2-3 idle.
+    setmaxnreg_dec<kRegsLow>();
+    producer_warps(tm, p, warp, sQ, sK, sV, q_full, kv_full, kv_empty, s_full, p_full, o_done, drain, abort_flag,
+                   tmem, head, q0, n_kv, limit);
+    tc_fence_before();
+    named_bar_sync(1, kThreads);
+    if (warp == 1) {
       tc_fence_after();
-      const float inv_l = l > 0.f ? 1.f / l : 0.f;
+      tmem_dealloc(tmem, 512);
+    }
+    return;
+  }
+  setmaxnreg_inc<kRegsHigh>();
+  // ------------------------------------------------------------ softmax (two warpgroups)
+  const int t = (warp - 4) >> 2;           // query tile handled by this warpgroup
+  const int quarter = warp & 3;            // TMEM lane quarter this warp may access
+  const int row = quarter * 32 + lane;
+  const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+  const uint32_t tS = tmem + t * 128 + lane_off;
+  const uint32_t tO = tmem + 256 + t * 128 + lane_off;
+  float m_used = -INFINITY, l = 0.f;
+  bool ok = true;
+  for (int j = 0; j < n_kv; ++j) {
+    if (!mbar_wait(&s_full[t], j & 1, limit, abort_flag)) {
+      ok = false;
+      break;
+    }
+    // O_t may be rescaled once PV_t of the previous tile completed (the
+    // commit order already implies it: S_t(j) was issued after PV_t(j-1)).
+    if (j > 0 && !mbar_wait(&o_done[t], (j - 1) & 1, limit, abort_flag)) {
+      ok = false;
+      break;
+    }
+    tc_fence_after();
+    const int kv_valid = p.T - j * kBKV;
+    // One TMEM read of the row; the max uses raw scores (the scale is positive).
+    uint32_t r[kBKV / 32][32];
+    load_row(tS, r);
+    if (kv_valid < kBKV) mask_row(r, kv_valid);
+    const float m_tile = row_max(r) * p.scale_log2;
+    const float m_new = fmaxf(m_used, m_tile);
+    const bool need = (j == 0) || (m_new > m_used + kRescaleThreshold);
+    const bool warp_need = __any_sync(0xffffffffu, need);
+    const float alpha = need ? ex2(m_used - m_new) : 1.f;
+    if (need) {
+      l *= alpha;
+      m_used = m_new;
+    }
+    tc_fence_after();
+    // P = 2^(s*scale - m) as packed bf16 pairs over the consumed S columns.
+    const float rowsum = kv_valid >= kBKV ? row_exp_pack<false, POLY>(tS, r, kv_valid, p.scale_log2, m_used)
+                                          : row_exp_pack<true, POLY>(tS, r, kv_valid, p.scale_log2, m_used);
+    l += rowsum;
+    // Rescale O_t after P is written (the S registers are dead by then, so
+    // the O chunk does not push the row past the register budget); PV_t(j)
+    // is issued only after p_full, i.e. after this.
+    if (warp_need && j > 0) {
 #pragma unroll
       for (int c = 0; c < kD / 16; ++c) {
-        uint32_t r[16];
-        tmem_ld16(tO + c * 16, r);
+        uint32_t o[16];
+        tmem_ld16(tO + c * 16, o);
         tmem_ld_wait();
-        if (q < p.T) {
-          uint4 a, b;
-          a.x = pack_bf16x2(__uint_as_float(r[0]) * inv_l, __uint_as_float(r[1]) * inv_l);
-          a.y = pack_bf16x2(__uint_as_float(r[2]) * inv_l, __uint_as_float(r[3]) * inv_l);
-          a.z = pack_bf16x2(__uint_as_float(r[4]) * inv_l, __uint_as_float(r[5]) * inv_l);
-          a.w = pack_bf16x2(__uint_as_float(r[6]) * inv_l, __uint_as_float(r[7]) * inv_l);
-          b.x = pack_bf16x2(__uint_as_float(r[8]) * inv_l, __uint_as_float(r[9]) * inv_l);
-          b.y = pack_bf16x2(__uint_as_float(r[10]) * inv_l, __uint_as_float(r[11]) * inv_l);
-          b.z = pack_bf16x2(__uint_as_float(r[12]) * inv_l, __uint_as_float(r[13]) * inv_l);
-          b.w = pack_bf16x2(__uint_as_float(r[14]) * inv_l, __uint_as_float(r[15]) * inv_l);
-          uint4* dst = reinterpret_cast<uint4*>(p.o + static_cast<long>(q) * p.H + head * kD + c * 16);
-          dst[0] = a;
-          dst[1] = b;
-        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+        tmem_st16(tO + c * 16, o);
       }
-      if (q < p.T) p.lse[static_cast<long>(head) * p.T + q] = (m_used + __log2f(l)) * 0.6931471805599453f;
-    } else if (n_kv > 0) {
-      if (lane == 0) report_status(p.status, kStatusTimeoutAccFull, blockIdx.x);
-      *abort_flag = 1;
     }
+    tmem_st_wait();
+    tc_fence_before();
+    mbar_arrive(&p_full[t]);
+  }
+  const int q = q0 + t * kBQ + row;
+  if (ok && n_kv > 0 && mbar_wait(&o_done[t], (n_kv - 1) & 1, limit, abort_flag)) {
+    tc_fence_after();
+    const float inv_l = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll
+    for (int c = 0; c < kD / 16; ++c) {
+      uint32_t r[16];
+      tmem_ld16(tO + c * 16, r);
+      tmem_ld_wait();
+      if (q < p.T) {
+        uint4 a, b;
+        a.x = pack_bf16x2(__uint_as_float(r[0]) * inv_l, __uint_as_float(r[1]) * inv_l);
+        a.y = pack_bf16x2(__uint_as_float(r[2]) * inv_l, __uint_as_float(r[3]) * inv_l);
+        a.z = pack_bf16x2(__uint_as_float(r[4]) * inv_l, __uint_as_float(r[5]) * inv_l);
+        a.w = pack_bf16x2(__uint_as_float(r[6]) * inv_l, __uint_as_float(r[7]) * inv_l);
+        b.x = pack_bf16x2(__uint_as_float(r[8]) * inv_l, __uint_as_float(r[9]) * inv_l);
+        b.y = pack_bf16x2(__uint_as_float(r[10]) * inv_l, __uint_as_float(r[11]) * inv_l);
+        b.z = pack_bf16x2(__uint_as_float(r[12]) * inv_l, __uint_as_float(r[13]) * inv_l);
+        b.w = pack_bf16x2(__uint_as_float(r[14]) * inv_l, __uint_as_float(r[15]) * inv_l);
+        uint4* dst = reinterpret_cast<uint4*>(p.o + static_cast<long>(q) * p.H + head * kD + c * 16);
+        dst[0] = a;
+        dst[1] = b;
+      }
+    }
+    if (q < p.T) p.lse[static_cast<long>(head) * p.T + q] = (m_used + __log2f(l)) * 0.6931471805599453f;
+  } else if (n_kv > 0) {
+    if (lane == 0) report_status(p.status, kStatusTimeoutAccFull, blockIdx.x);
+    *abort_flag = 1;
   }
 
   tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem, 512);
-  }
+  named_bar_sync(1, kThreads);
 }
 
 }  // namespace
@@ -462,8 +500,15 @@ std::vector<at::Tensor> attention_fwd(const at::Tensor& qkv, int64_t heads, int6
   static bool configured[64] = {false};
   const int device = qkv.get_device();
   if (!configured[device]) {
-    cudaFuncSetAttribute(attn_fwd_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
-    cudaFuncSetAttribute(attn_fwd_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    for (auto fn : {attn_fwd_kernel<0>, attn_fwd_kernel<4>}) {
+      cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+      // setmaxnreg.inc waits until the producer warpgroup has released enough
+      // registers; that only balances if the launch count is the assumed one.
+      cudaFuncAttributes attr{};
+      C10_CUDA_CHECK(cudaFuncGetAttributes(&attr, fn));
+      TORCH_CHECK(attr.numRegs == kLaunchRegs, "attention forward compiled with ", attr.numRegs,
+                  " registers per thread; the register split assumes ", kLaunchRegs);
+    }
     configured[device] = true;
   }
   // Exponential split: 0 = all on MUFU (default), 4 = one pair in four on the

@@ -1,0 +1,183 @@
+"""Collective sweep: peer-memory kernels against the NCCL path, with rooflines.
+
+``torchrun --nproc-per-node N -m h3_a100.bench_collectives --config
+configs/h3_fused_collective_sweep.yaml`` times, on every rank with CUDA events
+(after warm-up; the reported time is the max over ranks):
+
+* ``weight_gather``: one transformer block's frozen-weight unit, all-gathered
+  from the per-rank shards (NCCL ``all_gather_into_tensor`` vs the pull kernel);
+* ``adaln``: the row-sharded AdaLN projection of one block for the two
+  timestep rows (GEMV on the local rows + NCCL all-gather of the outputs, vs
+  the fused GEMV whose epilogue stores into every rank's output);
+* ``lora_step``: one role's optimizer step on the r128 LoRA of the config
+  (NCCL reduce-scatter + norm all-reduce + AdamW + all-gather, vs the single
+  cooperative peer-memory kernel).
+
+Each line carries the path's roofline: the slower of its HBM bytes at the
+measured copy bandwidth and its NVLink bytes per GPU at 770 GB/s per direction
+(the measured peer-copy rate on this hardware), and the achieved fraction.
+Reference counterparts: FSDP2's per-block all-gather, and
+``clip_grad_norm_`` + ``AdamW`` after FSDP2's reduce-scatter
+(``h3_a100/model.py:410-438``; ``h3_a100/trainer_loop.py:130-133,203-206``).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+from datetime import timedelta
+
+import torch
+import torch.distributed as dist
+
+NVLINK_GBS = 770.0
+
+
+def _peaks() -> dict:
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "MEASURED_PEAKS.json")
+    try:
+        with open(path) as fh:
+            return json.load(fh)
+    except OSError:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def _time(fn, iters: int, warmup: int = 3) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    dist.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(iters):
+        fn()
+    end.record()
+    torch.cuda.synchronize()
+    ms = torch.tensor([start.elapsed_time(end) / iters], device="cuda")
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    return float(ms.item())
+
+
+def main(argv=None) -> None:
+    p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    p.add_argument("--config", default=os.path.join("configs", "h3_fused_collective_sweep.yaml"))
+    p.add_argument("--iters", type=int, default=20)
+    p.add_argument("--which", default="nccl,p2p")
+    args = p.parse_args(argv)
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=timedelta(minutes=5), device_id=dev)
+    world, rank = dist.get_world_size(), dist.get_rank()
+
+    from .config import load_config
+    from .models.shared_backbone import dit_config_from
+    from .ops.native import NativeKernels
+    from .parallel.comm import TorchComm
+    from .parallel.p2p import PeerComm
+    from .trainer.optim import FlatAdamW
+
+    cfg = dit_config_from(load_config(args.config))
+    peaks = _peaks()
+    hbm = float(peaks["hbm_gbs"])
+    K = NativeKernels(dev)
+    h, f, dt = cfg.hidden, cfg.ffn, cfg.time_embed_dim
+    block_params = 3 * h * h + 3 * h + h * h + h + f * h + f + h * f + h
+    adaln_rows = 6 * h
+    rank_lora = 128
+    lora_numel = (cfg.num_blocks + cfg.num_refiner_blocks) * rank_lora * (10 * h + 2 * f)
+    comms = {}
+    if "nccl" in args.which:
+        comms["nccl"] = TorchComm(dist.group.WORLD, dev)
+    if "p2p" in args.which and world > 1:
+        comms["p2p"] = PeerComm(dist.group.WORLD, dev, kernels=K)
+    lines = []
+
+    def emit(op, impl, ms, hbm_bytes, link_bytes, extra=None):
+        roof_ms = max(hbm_bytes / (hbm * 1e9), link_bytes / (NVLINK_GBS * 1e9)) * 1e3
+        line = {"op": op, "impl": impl, "n_gpus": world, "ms": round(ms, 4),
+                "roofline_ms": round(roof_ms, 4), "frac_of_roofline": round(roof_ms / ms, 3) if ms > 0 else None,
+                "hbm_bytes": int(hbm_bytes), "nvlink_bytes_per_gpu": int(link_bytes)}
+        if extra:
+            line.update(extra)
+        lines.append(line)
+
+    for impl, comm in comms.items():
+        # ---- per-block frozen-weight all-gather (bf16)
+        quantum = world * 64
+        padded = (block_params + quantum - 1) // quantum * quantum
+        shard = comm.alloc_shard(padded // world, torch.bfloat16)
+        shard.normal_()
+
+        def gather():
+            out = comm.wait(comm.all_gather_async(shard, padded))
+            comm.recycle(out)
+
+        ms = _time(gather, args.iters)
+        nbytes = padded * 2
+        emit("weight_gather", impl, ms, hbm_bytes=nbytes + nbytes / world,
+             link_bytes=nbytes * (world - 1) / world, extra={"unit_bytes": nbytes})
+
+        # ---- AdaLN projection (row-sharded) for two timestep rows
+        rows = adaln_rows // world
+        w_rows = (torch.randn(rows, dt, device=dev) * 0.02).to(torch.bfloat16)
+        b_rows = torch.zeros(rows, device=dev, dtype=torch.bfloat16)
+        temb = torch.randn(2, dt, device=dev).to(torch.bfloat16)
+        if impl == "p2p":
+            out = comm.alloc_symmetric(2 * world * rows, torch.float32).view(2, world * rows)
+
+            def adaln():
+                comm.adaln_project(temb, w_rows, b_rows, out)
+        else:
+            def adaln():
+                local_rows = K.adaln_project(temb, w_rows, b_rows)
+                comm.all_gather_rows(local_rows)
+
+        ms = _time(adaln, args.iters)
+        emit("adaln", impl, ms, hbm_bytes=rows * dt * 2, link_bytes=2 * rows * 4 * (world - 1))
+        if impl == "p2p":
+            comm.check_status()
+
+        # ---- LoRA optimizer step (one role)
+        class _Store:
+            def __init__(self, flat, grad):
+                self.flat, self.grad = flat, grad
+
+            def ensure_grad(self):
+                return self.grad
+
+            def zero_grad(self):
+                self.grad.zero_()
+
+        n = (lora_numel + 4 * world - 1) // (4 * world) * (4 * world)
+        flat = comm.alloc_symmetric(n, torch.bfloat16)
+        grad = comm.alloc_symmetric(n, torch.float32)
+        flat.normal_()
+        grad.normal_()
+        opt = FlatAdamW(_Store(flat, grad), lr=1e-4, weight_decay=0.01, max_grad_norm=1.0, kernels=K, comm=comm,
+                        shard_states=True)
+
+        ms = _time(lambda: opt.step(1e-4), max(3, args.iters // 4))
+        chunk = n // world
+        # HBM: read world fp32 grad chunks (local part) + write chunk, master/m/v read+write, bf16 param stores
+        hbm_bytes = chunk * 4 * 2 + chunk * 4 * 6 + n * 2
+        link = (world - 1) * chunk * 4 + (world - 1) * chunk * 2
+        emit("lora_step", impl, ms, hbm_bytes=hbm_bytes, link_bytes=link, extra={"params": n, "fused": opt.fused})
+        if impl == "p2p":
+            comm.check_status()
+        K.check_status()
+        del shard, flat, grad, opt
+        torch.cuda.synchronize()
+        dist.barrier()
+
+    if rank == 0:
+        for line in lines:
+            print(json.dumps(line), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
