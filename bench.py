@@ -162,6 +162,7 @@ def main() -> None:
                 "global_batch": world,
                 "seq_len": tokens,
                 "parallelism": f"fsdp{world}" if world > 1 else "single",
+                "comm": getattr(trainer.comm, "name", "none") if world > 1 else "none",
                 "cycle": "Student x1 + Fake x5 (24/6/1 forwards, 1/5 backwards), 300 boundary copies",
                 "l2": "no flush: every cycle streams 66 GB of weights, far larger than the 126 MB L2",
                 "headline_config": headline,

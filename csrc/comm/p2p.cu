@@ -106,6 +106,20 @@ __device__ bool grid_barrier(int* bar, uint64_t limit_ns) {
   return s_ok != 0;
 }
 
+// NVLink SHARP (NVLS) through NVSwitch: a load from a multicast address returns
+// the element-wise sum over every GPU bound to it; a store is written to all.
+__device__ __forceinline__ float4 multimem_ld_add_v4(const float* mc) {
+  float4 v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(mc)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ void multimem_st_v2_bf16x2(__nv_bfloat16* mc, uint32_t a, uint32_t b) {
+  asm volatile("multimem.st.relaxed.sys.global.v2.bf16x2 [%0], {%1, %2};" ::"l"(mc), "r"(a), "r"(b) : "memory");
+}
+
 __device__ __forceinline__ float block_sum256(float v) {
   __shared__ float part[32];
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -119,14 +133,29 @@ __device__ __forceinline__ float block_sum256(float v) {
 }
 
 // ------------------------------------------------------------------ all-gather (pull)
+// Each thread keeps kUnroll 16-byte peer loads in flight before storing them
+// (NVLink reads need many bytes outstanding to reach link bandwidth).
+constexpr int kPullUnroll = 4;
 __global__ void all_gather_pull_kernel(PeerPtrs src, int world, long shard_bytes, uint8_t* __restrict__ dst) {
   const long units_per_shard = shard_bytes >> 4;
   const long total = units_per_shard * world;
-  for (long u = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; u < total;
-       u += static_cast<long>(gridDim.x) * blockDim.x) {
-    const int owner = static_cast<int>(u / units_per_shard);
-    const long local = u - owner * units_per_shard;
-    reinterpret_cast<uint4*>(dst)[u] = reinterpret_cast<const uint4*>(src.p[owner])[local];
+  const long stride = static_cast<long>(gridDim.x) * blockDim.x;
+  for (long base = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; base < total;
+       base += stride * kPullUnroll) {
+    uint4 v[kPullUnroll];
+#pragma unroll
+    for (int k = 0; k < kPullUnroll; ++k) {
+      const long u = base + k * stride;
+      if (u < total) {
+        const int owner = static_cast<int>(u / units_per_shard);
+        v[k] = reinterpret_cast<const uint4*>(src.p[owner])[u - owner * units_per_shard];
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kPullUnroll; ++k) {
+      const long u = base + k * stride;
+      if (u < total) reinterpret_cast<uint4*>(dst)[u] = v[k];
+    }
   }
 }
 
@@ -136,6 +165,8 @@ struct LoraParams {
   PeerPtrs param;   // bf16 [n_pad] per rank (replicated compute copy)
   PeerPtrs flags;   // int32 signal buffers
   const int* my_flags;
+  const float* mc_grad;       // multicast (NVLS) address of the gradient buffer, or null
+  __nv_bfloat16* mc_param;    // multicast address of the parameter buffer, or null
   float* master;    // fp32 [chunk] (this rank's shard)
   float* m;
   float* v;
@@ -163,25 +194,50 @@ __global__ void __launch_bounds__(256) lora_rs_adamw_kernel(LoraParams p) {
   float* my_grad = reinterpret_cast<float*>(p.grad.p[p.rank]);
   float ss = 0.f;
   const long n4 = p.chunk >> 2;
-  for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n4;
-       i += static_cast<long>(gridDim.x) * blockDim.x) {
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  const long stride = static_cast<long>(gridDim.x) * blockDim.x;
+  constexpr int kU = 4;   // float4 units in flight per thread
+  for (long base = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; base < n4; base += stride * kU) {
+    float4 acc[kU];
+    if (p.mc_grad != nullptr) {
+      // the switch sums the world's copies: one chunk crosses NVLink, not world-1
 #pragma unroll
-    for (int r = 0; r < kMaxRanks; ++r) {
-      if (r < p.world) {
-        const float4 g = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.grad.p[r]) + lo)[i];
-        acc.x += g.x;
-        acc.y += g.y;
-        acc.z += g.z;
-        acc.w += g.w;
+      for (int k = 0; k < kU; ++k)
+        acc[k] = base + k * stride < n4 ? multimem_ld_add_v4(p.mc_grad + lo + 4 * (base + k * stride))
+                                        : make_float4(0.f, 0.f, 0.f, 0.f);
+    } else {
+#pragma unroll
+      for (int k = 0; k < kU; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int r = 0; r < kMaxRanks; ++r) {
+        if (r < p.world) {
+          const float4* src = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.grad.p[r]) + lo);
+          float4 g[kU];
+#pragma unroll
+          for (int k = 0; k < kU; ++k)
+            g[k] = base + k * stride < n4 ? src[base + k * stride] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int k = 0; k < kU; ++k) {
+            acc[k].x += g[k].x;
+            acc[k].y += g[k].y;
+            acc[k].z += g[k].z;
+            acc[k].w += g[k].w;
+          }
+        }
       }
     }
-    acc.x *= p.inv_world;
-    acc.y *= p.inv_world;
-    acc.z *= p.inv_world;
-    acc.w *= p.inv_world;
-    reinterpret_cast<float4*>(my_grad + lo)[i] = acc;
-    ss += acc.x * acc.x + acc.y * acc.y + acc.z * acc.z + acc.w * acc.w;
+#pragma unroll
+    for (int k = 0; k < kU; ++k) {
+      const long i = base + k * stride;
+      if (i < n4) {
+        float4 a = acc[k];
+        a.x *= p.inv_world;
+        a.y *= p.inv_world;
+        a.z *= p.inv_world;
+        a.w *= p.inv_world;
+        reinterpret_cast<float4*>(my_grad + lo)[i] = a;
+        ss += a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w;
+      }
+    }
   }
   ss = block_sum256(ss);
   if (threadIdx.x == 0) atomicAdd(p.scratch, ss);
@@ -237,9 +293,13 @@ __global__ void __launch_bounds__(256) lora_rs_adamw_kernel(LoraParams p) {
     uint2 packed;
     packed.x = pack_bf16x2(w[0], w[1]);
     packed.y = pack_bf16x2(w[2], w[3]);
+    if (p.mc_param != nullptr) {
+      multimem_st_v2_bf16x2(p.mc_param + lo + 4 * i, packed.x, packed.y);   // one store reaches every replica
+    } else {
 #pragma unroll
-    for (int r = 0; r < kMaxRanks; ++r)
-      if (r < p.world) reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(p.param.p[r]) + lo)[i] = packed;
+      for (int r = 0; r < kMaxRanks; ++r)
+        if (r < p.world) reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(p.param.p[r]) + lo)[i] = packed;
+    }
   }
   if (!grid_barrier(p.bar, p.status.limit_ns)) {
     if (threadIdx.x == 0) report_status(p.status, kStatusTimeoutPeer, 13);
@@ -345,7 +405,7 @@ void lora_rs_adamw(const std::vector<int64_t>& grad_ptrs, const std::vector<int6
                    const std::vector<int64_t>& flag_ptrs, int64_t rank, int64_t epoch, const at::Tensor& master,
                    const at::Tensor& m, const at::Tensor& v, const at::Tensor& scratch, const at::Tensor& bar,
                    double lr, double b1, double b2, double eps, double wd, int64_t step, double max_norm,
-                   const at::Tensor& status, int64_t limit_ns) {
+                   const at::Tensor& status, int64_t limit_ns, int64_t mc_grad, int64_t mc_param) {
   const int world = static_cast<int>(grad_ptrs.size());
   TORCH_CHECK(param_ptrs.size() == grad_ptrs.size() && flag_ptrs.size() == grad_ptrs.size(), "peer lists");
   TORCH_CHECK(master.scalar_type() == at::kFloat && m.sizes() == master.sizes() && v.sizes() == master.sizes(),
@@ -359,6 +419,9 @@ void lora_rs_adamw(const std::vector<int64_t>& grad_ptrs, const std::vector<int6
   p.param = peers_of(param_ptrs);
   p.flags = peers_of(flag_ptrs);
   p.my_flags = reinterpret_cast<const int*>(flag_ptrs[rank]);
+  TORCH_CHECK(mc_grad % 16 == 0 && mc_param % 16 == 0, "multicast addresses must be 16-byte aligned");
+  p.mc_grad = reinterpret_cast<const float*>(mc_grad);
+  p.mc_param = reinterpret_cast<__nv_bfloat16*>(mc_param);
   p.master = master.data_ptr<float>();
   p.m = m.data_ptr<float>();
   p.v = v.data_ptr<float>();
@@ -379,11 +442,14 @@ void lora_rs_adamw(const std::vector<int64_t>& grad_ptrs, const std::vector<int6
   p.inv_world = 1.f / static_cast<float>(world);
   p.status = status_of(status, limit_ns);
   cudaMemsetAsync(p.scratch, 0, sizeof(float), stream);
-  int per_sm = 0;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, lora_rs_adamw_kernel, 256, 0);
-  cudaDeviceProp prop;
-  cudaGetDeviceProperties(&prop, device);
-  const int grid = std::max(1, std::min(per_sm, 4)) * prop.multiProcessorCount;
+  static int grid_for_device[64] = {0};
+  if (grid_for_device[device] == 0) {
+    int per_sm = 0, sms = 0;
+    C10_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, lora_rs_adamw_kernel, 256, 0));
+    C10_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+    grid_for_device[device] = std::max(1, std::min(per_sm, 4)) * sms;
+  }
+  const int grid = grid_for_device[device];
   void* args[] = {&p};
   const cudaError_t err = cudaLaunchCooperativeKernel(reinterpret_cast<void*>(lora_rs_adamw_kernel), grid, 256,
                                                       args, 0, stream);

@@ -11,7 +11,7 @@ void lora_rs_adamw(const std::vector<int64_t>& grad_ptrs, const std::vector<int6
                    const std::vector<int64_t>& flag_ptrs, int64_t rank, int64_t epoch, const at::Tensor& master,
                    const at::Tensor& m, const at::Tensor& v, const at::Tensor& scratch, const at::Tensor& bar,
                    double lr, double b1, double b2, double eps, double wd, int64_t step, double max_norm,
-                   const at::Tensor& status, int64_t limit_ns);
+                   const at::Tensor& status, int64_t limit_ns, int64_t mc_grad, int64_t mc_param);
 void adaln_project_gather(const at::Tensor& temb, const at::Tensor& w, const c10::optional<at::Tensor>& b,
                           const std::vector<int64_t>& out_ptrs, const std::vector<int64_t>& flag_ptrs, int64_t rank,
                           int64_t epoch, int64_t slot, const at::Tensor& status, int64_t limit_ns);

@@ -36,8 +36,9 @@ def _init(rank: int, port: int) -> torch.device:
     return dev
 
 
-def _collectives(rank: int, port: int, errors) -> None:
+def _collectives(rank: int, port: int, errors, multimem: str = "0") -> None:
     try:
+        os.environ["H3_P2P_MULTIMEM"] = multimem
         dev = _init(rank, port)
         from h3_a100.ops.native import NativeKernels
         from h3_a100.ops.torch_kernels import TorchKernels
@@ -141,10 +142,10 @@ def _cycle(rank: int, port: int, comm_kind: str, results, errors) -> None:
             dist.destroy_process_group()
 
 
-def _spawn(fn, port):
+def _spawn(fn, port, *extra):
     ctx = mp.get_context("spawn")
     errors = ctx.Queue()
-    procs = [ctx.Process(target=fn, args=(r, port, errors)) for r in range(WORLD)]
+    procs = [ctx.Process(target=fn, args=(r, port, errors, *extra)) for r in range(WORLD)]
     for p in procs:
         p.start()
     for p in procs:
@@ -164,8 +165,11 @@ def two_gpus():
         pytest.skip("needs two GPUs")
 
 
-def test_peer_collectives_match_nccl(two_gpus):
-    msgs, codes = _spawn(_collectives, _free_port())
+@pytest.mark.parametrize("multimem", ["0", "1"], ids=["unicast", "multimem"])
+def test_peer_collectives_match_nccl(two_gpus, multimem):
+    """Unicast peer loads/stores, and the NVLS multimem variant (falls back to
+    unicast where the fabric has no multicast objects)."""
+    msgs, codes = _spawn(_collectives, _free_port(), multimem)
     assert not msgs, "\n".join(msgs)
     assert codes == [0] * WORLD
 
