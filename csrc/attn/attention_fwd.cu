@@ -73,21 +73,47 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// Packed f32x2 arithmetic (sm_100): one instruction for two lanes of a pair.
+__device__ __forceinline__ uint64_t pack2(float a, float b) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(a), "f"(b));
+  return d;
+}
+__device__ __forceinline__ void unpack2(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 // 2^x on the FMA pipe, to take part of the exponentials off the MUFU unit:
 // x = n + f with n = round(x) (magic-number add, no conversion instruction)
 // and f in [-1/2, 1/2]; 2^f is a cubic least-squares fit at Chebyshev nodes
 // (max relative error 1.0e-4, below bf16 resolution); 2^n is added to the
 // exponent field.  Valid for x >= -126 (inputs are clamped).
-__device__ __forceinline__ float exp2_fma(float x) {
-  x = fmaxf(x, -126.0f);
-  const float magic = 12582912.0f;  // 1.5 * 2^23
-  const float t = x + magic;
-  const int n = __float_as_int(t) - 0x4B400000;
-  const float f = x - (t - magic);
-  float p = fmaf(0.05592203512787819f, f, 0.24264007806777954f);
-  p = fmaf(p, f, 0.6931210160255432f);
-  p = fmaf(p, f, 0.9999244809150696f);
-  return __int_as_float(__float_as_int(p) + (n << 23));
+// Applied to a pair with packed f32x2 arithmetic (one FADD2 / FFMA2 per step
+// for both lanes), which halves the issue slots of the FMA-pipe share.
+__device__ __forceinline__ void exp2_fma2(float xa, float xb, float& ra, float& rb) {
+  const uint64_t x2 = pack2(fmaxf(xa, -126.0f), fmaxf(xb, -126.0f));
+  const uint64_t t2 = add2(x2, pack2(12582912.0f, 12582912.0f));     // round to nearest: n in the low bits
+  const uint64_t n2 = add2(t2, pack2(-12582912.0f, -12582912.0f));   // n as a float
+  const uint64_t f2 = fma2(n2, pack2(-1.0f, -1.0f), x2);              // f = x - n in [-1/2, 1/2]
+  uint64_t q2 = fma2(pack2(0.05592203512787819f, 0.05592203512787819f), f2,
+                     pack2(0.24264007806777954f, 0.24264007806777954f));
+  q2 = fma2(q2, f2, pack2(0.6931210160255432f, 0.6931210160255432f));
+  q2 = fma2(q2, f2, pack2(0.9999244809150696f, 0.9999244809150696f));
+  float qa, qb, ta, tb;
+  unpack2(q2, qa, qb);
+  unpack2(t2, ta, tb);
+  ra = __int_as_float(__float_as_int(qa) + (__float_as_int(ta) << 23));
+  rb = __int_as_float(__float_as_int(qb) + (__float_as_int(tb) << 23));
 }
 
 // 32 lanes x 32 bit, 32 consecutive columns per thread.
@@ -116,26 +142,6 @@ __device__ __forceinline__ void setmaxnreg_inc() {
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-  return d;
-}
-
-// Packed f32x2 arithmetic (sm_100): one instruction for two lanes of a pair.
-__device__ __forceinline__ uint64_t pack2(float a, float b) {
-  uint64_t d;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(a), "f"(b));
-  return d;
-}
-__device__ __forceinline__ void unpack2(uint64_t v, float& a, float& b) {
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
-}
-__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-  return d;
-}
-__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
 
@@ -172,8 +178,10 @@ __device__ __forceinline__ float row_max(const uint32_t (&r)[kBKV / 32][32]) {
 
 // P = 2^(s*scale - m) from the registers, stored as packed bf16 pairs over the
 // first 64 S columns; returns the row sum.  The scale/offset and the sum use
-// packed f32x2 instructions (four independent pair accumulators).  POLY > 0
-// sends one pair in POLY through the FMA-pipe exponential, the rest to MUFU.
+// packed f32x2 instructions (four independent pair accumulators).  POLY of
+// every 8 pairs go through the FMA-pipe exponential, the rest to MUFU: MUFU
+// takes 8 cycles per warp instruction, so at POLY = 0 the exponentials alone
+// are ~1,024 cycles per KV tile and warp, on the softmax's critical path.
 template <bool MASKED, int POLY>
 __device__ __forceinline__ float row_exp_pack(uint32_t tS, const uint32_t (&r)[kBKV / 32][32], int valid, float scale,
                                               float m) {
@@ -188,9 +196,13 @@ __device__ __forceinline__ float row_exp_pack(uint32_t tS, const uint32_t (&r)[k
     for (int i = 0; i < 16; ++i) {
       float xa, xb;
       unpack2(fma2(pack2(__uint_as_float(r[c][2 * i]), __uint_as_float(r[c][2 * i + 1])), scale2, negm2), xa, xb);
-      const bool poly = POLY > 0 && (i % (POLY > 0 ? POLY : 1)) == (POLY > 0 ? POLY - 1 : 0);
-      float a = poly ? exp2_fma(xa) : ex2(xa);
-      float b = poly ? exp2_fma(xb) : ex2(xb);
+      float a, b;
+      if ((i & 7) < POLY) {
+        exp2_fma2(xa, xb, a, b);
+      } else {
+        a = ex2(xa);
+        b = ex2(xb);
+      }
       if (MASKED) {
         const int k0 = c * 32 + 2 * i;
         a = k0 < valid ? a : 0.f;
@@ -500,7 +512,7 @@ std::vector<at::Tensor> attention_fwd(const at::Tensor& qkv, int64_t heads, int6
   static bool configured[64] = {false};
   const int device = qkv.get_device();
   if (!configured[device]) {
-    for (auto fn : {attn_fwd_kernel<0>, attn_fwd_kernel<4>}) {
+    for (auto fn : {attn_fwd_kernel<0>, attn_fwd_kernel<2>, attn_fwd_kernel<3>, attn_fwd_kernel<4>}) {
       cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
       // setmaxnreg.inc waits until the producer warpgroup has released enough
       // registers; that only balances if the launch count is the assumed one.
@@ -511,17 +523,20 @@ std::vector<at::Tensor> attention_fwd(const at::Tensor& qkv, int64_t heads, int6
     }
     configured[device] = true;
   }
-  // Exponential split: 0 = all on MUFU (default), 4 = one pair in four on the
-  // FMA pipe.  H3_ATTN_FWD_POLY selects it for measurements only.
+  // Exponential split: POLY of every 8 pairs on the FMA pipe (0, 2, 3, 4).
+  // H3_ATTN_FWD_POLY selects it for measurements only.
   static const int poly = [] {
     const char* v = std::getenv("H3_ATTN_FWD_POLY");
     return v != nullptr ? std::atoi(v) : 0;
   }();
   dim3 grid(static_cast<unsigned>((T + kQTiles * kBQ - 1) / (kQTiles * kBQ)), static_cast<unsigned>(heads));
-  if (poly == 4)
-    attn_fwd_kernel<4><<<grid, kThreads, kSmem, at::cuda::getCurrentCUDAStream(device).stream()>>>(tm, p);
-  else
-    attn_fwd_kernel<0><<<grid, kThreads, kSmem, at::cuda::getCurrentCUDAStream(device).stream()>>>(tm, p);
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream(device).stream();
+  switch (poly) {
+    case 2: attn_fwd_kernel<2><<<grid, kThreads, kSmem, stream>>>(tm, p); break;
+    case 3: attn_fwd_kernel<3><<<grid, kThreads, kSmem, stream>>>(tm, p); break;
+    case 4: attn_fwd_kernel<4><<<grid, kThreads, kSmem, stream>>>(tm, p); break;
+    default: attn_fwd_kernel<0><<<grid, kThreads, kSmem, stream>>>(tm, p); break;
+  }
   note_launch();
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {o, lse};
