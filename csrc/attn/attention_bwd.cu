@@ -18,10 +18,14 @@
 //             dQ_i = dS K                               (smem A, MN-major), two
 //                    N = 64 halves in the TMEM columns S^T / dP^T leave free
 //             dV  += P^T dO_i,  dK += dS^T Q_i          (A from TMEM, .ts form)
-//           the same warps then read dQ_i out of TMEM (half of it each) while the
-//           tensor core runs the dV/dK MMAs, stage it in the consumed dS^T buffer
-//           and add it into an fp32 accumulator with TMA bulk tensor reduce-adds
-//           (whole 128-byte lines; 16-byte red.add was the bottleneck);
+//           the same warps then read dQ_i out of TMEM (half of it each), stage
+//           it in the stage buffer whose Q_i / dO_i the dV/dK MMAs just finished
+//           reading, and add it into an fp32 accumulator with TMA bulk tensor
+//           reduce-adds (whole 128-byte lines; 16-byte red.add was slower).  The
+//           wait for the reduces' smem reads is deferred by one step (until
+//           after the next softmax), then the stage is handed back to the loader:
+//           waiting right away put the reduce latency on the critical path
+//           (121.7 ms -> 100.6 ms at T = 37,730, 42 heads);
 //           warp 0 streams Q_i, dO_i, lse2_i, delta_i (2 stages), warp 1 issues
 //           the MMAs.  dV/dK are written once at the end.
 //   finish  dq = bf16(dQ accumulator)
@@ -183,7 +187,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* dq_empty = bars + 8;
   uint64_t* acc_done = bars + 9;
   uint64_t* drain = bars + 10;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+  uint64_t* stage_read = bars + 11;  // [2] the MMAs finished reading Q_i / dO_i of a stage
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id(), lane = lane_id();
@@ -200,7 +205,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(kv_full, 1);
     for (int s = 0; s < 2; ++s) {
       mbar_init(&qd_full[s], 1);
-      mbar_init(&qd_empty[s], 1);
+      mbar_init(&qd_empty[s], 2);    // each warpgroup, once its dQ reduces have read the stage
+      mbar_init(&stage_read[s], 1);
     }
     mbar_init(s_full, 1);
     mbar_init(p_full, 256);
@@ -310,7 +316,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int ks = 0; ks < kB / 16; ++ks)
           umma_f16_ts(tDK, tDP + ks * 8, umma_smem_desc(q_base + ks * 2048, kChunk, 1024), kIdescTS,
                       (i > 0 || ks > 0) ? 1u : 0u);
-        umma_commit(&qd_empty[st]);
+        umma_commit(&stage_read[st]);
       }
       if (ok) umma_commit(acc_done);
       if (!ok) {
@@ -338,6 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool key_valid = k0 + row < p.T;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     bool ok = true;
+    const bool reducer = quarter == 0 && lane == 0;   // issues this warpgroup's dQ reduces
     for (int i = 0; i < n_q; ++i) {
       const int st = i & 1;
       if (!mbar_wait(s_full, i & 1, limit, abort_flag)) { ok = false; break; }
@@ -399,40 +406,50 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(p_full);
       // dQ_i (rows = queries): this warpgroup's 64 columns as two 32-column fp32
-      // boxes, staged in its 16 KB half of the (now consumed) dS^T buffer in the
-      // 128B-swizzled layout and added into the accumulator by a TMA bulk reduce.
+      // boxes, staged in the 128B-swizzled layout in the stage that held Q_i
+      // (warpgroup 0) or dO_i (warpgroup 1) -- free once the dV / dK MMAs read
+      // it -- and added into the accumulator by TMA bulk reduces whose smem
+      // reads are waited for only one step later, after that step's softmax.
+      if (reducer && i > 0) {
+        // The previous step's reduces read their stage while this step's
+        // MMAs and softmax ran; once read, the loader may refill that stage.
+        bulk_wait_read_all();
+        mbar_arrive(&qd_empty[(i - 1) & 1]);
+      }
       if (!mbar_wait(dq_full, i & 1, limit, abort_flag)) { ok = false; break; }
+      if (!mbar_wait(&stage_read[st], (i >> 1) & 1, limit, abort_flag)) { ok = false; break; }
       tc_fence_after();
-      {
-        uint8_t* stage = sDS + half * (kTile / 2);
+      if (!(p.ablate & 1)) {
+        uint8_t* stage = sStage + st * kStageBytes + half * kTile;
         const uint32_t src = (half == 0 ? tS : tDP) + 64 + lane_off;
 #pragma unroll
         for (int box = 0; box < 2; ++box) {
           uint32_t r[32];
           tmem_ld32(src + box * 32, r);
           tmem_ld_wait();
-          if (!(p.ablate & 1)) {
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-              uint4 v;
-              v.x = r[u * 4];
-              v.y = r[u * 4 + 1];
-              v.z = r[u * 4 + 2];
-              v.w = r[u * 4 + 3];
-              *reinterpret_cast<uint4*>(stage + row * 128 + ((u ^ (row & 7)) << 4)) = v;
-            }
-            fence_async_smem();
-            named_sync(2 + half, 128);
-            if (quarter == 0 && lane == 0) {
-              tma_reduce_add_2d(&tm_dq, stage, head * kD + half * 64 + box * 32, i * kB);
-              bulk_wait_read_all();
-            }
-            named_sync(2 + half, 128);
+          for (int u = 0; u < 8; ++u) {
+            uint4 v;
+            v.x = r[u * 4];
+            v.y = r[u * 4 + 1];
+            v.z = r[u * 4 + 2];
+            v.w = r[u * 4 + 3];
+            *reinterpret_cast<uint4*>(stage + box * (kTile / 2) + row * 128 + ((u ^ (row & 7)) << 4)) = v;
           }
+        }
+        fence_async_smem();
+        named_sync(2 + half, 128);
+        if (reducer) {
+          tma_reduce_add_2d(&tm_dq, stage, head * kD + half * 64, i * kB);
+          tma_reduce_add_2d(&tm_dq, stage + kTile / 2, head * kD + half * 64 + 32, i * kB);
         }
       }
       tc_fence_before();
       mbar_arrive(dq_empty);
+    }
+    if (reducer) {
+      bulk_wait_read_all();   // no reduce still reads this CTA's smem at exit
+      if (ok && n_q > 0) mbar_arrive(&qd_empty[(n_q - 1) & 1]);
     }
     // final dV (warpgroup 0) / dK (warpgroup 1) rows -> dqkv
     if (ok && n_q > 0 && mbar_wait(acc_done, 0, limit, abort_flag)) {
