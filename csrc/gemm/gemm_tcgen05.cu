@@ -21,6 +21,7 @@
 //   error code, drains its own TMA loads / MMAs, frees TMEM and returns.
 // * Every TMA load in this file targets one CTA only.
 #include <ATen/cuda/CUDAContext.h>
+#include <cstdlib>
 #include <c10/cuda/CUDAGuard.h>
 #include <cudaTypedefs.h>
 #include <torch/extension.h>
@@ -64,6 +65,8 @@ struct GemmParams {
   const __nv_bfloat16* pre;
   long ldp;
   float alpha;
+  int tma_store;  // bf16 outputs leave through smem + TMA tensor stores (full 128-byte lines)
+  int ablate;     // diagnostic only (H3_GEMM_ABLATE): 1 = skip the epilogue's global stores
   KernelStatus status;
 };
 
@@ -73,7 +76,10 @@ struct Cfg {
   static constexpr int kABytes = BM * BK * 2;
   static constexpr int kBBytes = BN * BK * 2;
   static constexpr int kTmemCols = 2 * BN;
-  static constexpr int kSmem = 1024 + kStages * (kABytes + kBBytes) + 256;
+  // epilogue staging: 4 warps x 2 slots x (32 rows x 64 bf16 columns)
+  static constexpr int kEpiSlotBytes = 32 * 64 * 2;
+  static constexpr int kEpiBytes = 4 * 2 * kEpiSlotBytes;
+  static constexpr int kSmem = 1024 + kStages * (kABytes + kBBytes) + kEpiBytes + 256;
 };
 
 __device__ __forceinline__ float gelu_tanh_f(float x) {
@@ -136,10 +142,145 @@ __device__ __forceinline__ void load_row16_bf16(const __nv_bfloat16* src, float 
   }
 }
 
+// Output values of 16 consecutive columns of row m for the bf16 epilogues
+// (v -> out; g -> out2 for GELU).  Columns past N come out as 0.
+template <int EPI>
+__device__ __forceinline__ void epilogue_vals(const GemmParams& p, int m, int n, const uint32_t (&r)[16],
+                                              float (&v)[16], float (&g)[16], const float* aux = nullptr) {
+  const int valid = min(16, p.N - n);
+  if (valid <= 0) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = g[j] = 0.0f;
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+  float bias[16];
+  if (p.bias != nullptr) {
+    load_row16_bf16(p.bias + n, bias, valid);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) bias[j] = 0.0f;
+  }
+  if constexpr (EPI == kEpiBf16) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = p.alpha * v[j] + bias[j];
+  } else if constexpr (EPI == kEpiGelu) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      v[j] = bf16_round(v[j] + bias[j]);
+      g[j] = gelu_tanh_f(v[j]);
+    }
+  } else if constexpr (EPI == kEpiRope) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = bf16_round(v[j] + bias[j]);
+    if (n < p.rope_cols) {
+      // the 16 columns sit inside one head (n and head_dim are multiples of 16):
+      // their 8 rotation pairs use 8 consecutive table entries (two float4 loads)
+      const int half = p.head_dim >> 1;
+      const int base = (n % p.head_dim) >> 1;
+      const float4* cs = reinterpret_cast<const float4*>(p.cos_t + static_cast<long>(m) * half + base);
+      const float4* sn = reinterpret_cast<const float4*>(p.sin_t + static_cast<long>(m) * half + base);
+      const float4 c0 = cs[0], c1 = cs[1], s0 = sn[0], s1 = sn[1];
+      const float cv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+      const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float a = v[2 * j], b = v[2 * j + 1];
+        v[2 * j] = a * cv[j] - b * sv[j];
+        v[2 * j + 1] = a * sv[j] + b * cv[j];
+      }
+    }
+  } else if constexpr (EPI == kEpiGatedRes) {
+    float res[16];
+    if (aux != nullptr) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) res[j] = aux[j];
+    } else {
+      load_row16_bf16(p.res + static_cast<long>(m) * p.ldr + n, res, valid);
+    }
+    const float* gate = p.gate + (m >= p.split_row ? p.ldg : 0) + n;
+    float gt[16];
+    if (valid == 16 && (reinterpret_cast<uintptr_t>(gate) & 15u) == 0) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 g4 = reinterpret_cast<const float4*>(gate)[q];
+        gt[4 * q] = g4.x;
+        gt[4 * q + 1] = g4.y;
+        gt[4 * q + 2] = g4.z;
+        gt[4 * q + 3] = g4.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) gt[j] = j < valid ? gate[j] : 0.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float y = bf16_round(v[j] + bias[j]);
+      v[j] = res[j] + gt[j] * y;
+    }
+  } else if constexpr (EPI == kEpiGeluBwd) {
+    float pre[16];
+    if (aux != nullptr) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) pre[j] = aux[j];
+    } else {
+      load_row16_bf16(p.pre + static_cast<long>(m) * p.ldp + n, pre, valid);
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = bf16_round(v[j]) * gelu_tanh_grad_f(pre[j]);
+  }
+}
+
+__device__ __forceinline__ void fence_async_smem_cta() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// 16 bf16 values of `row` (columns 16*group ..) from a 128B-swizzled 32 x 64 staging tile.
+__device__ __forceinline__ void unstage16(const uint8_t* slot, int row, int group, float (&v)[16]) {
+  const int u0 = 2 * group, u1 = 2 * group + 1;
+  const uint4 a = *reinterpret_cast<const uint4*>(slot + row * 128 + ((u0 ^ (row & 7)) << 4));
+  const uint4 b = *reinterpret_cast<const uint4*>(slot + row * 128 + ((u1 ^ (row & 7)) << 4));
+  const __nv_bfloat16* pa = reinterpret_cast<const __nv_bfloat16*>(&a);
+  const __nv_bfloat16* pb = reinterpret_cast<const __nv_bfloat16*>(&b);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    v[j] = __bfloat162float(pa[j]);
+    v[8 + j] = __bfloat162float(pb[j]);
+  }
+}
+
+// 16 bf16 values as two 16-byte units of a 128B-swizzled 32 x 64 staging tile.
+__device__ __forceinline__ void stage16(uint8_t* slot, int row, int group, const float (&v)[16]) {
+  uint4 a, b;
+  a.x = pack_bf16x2(v[0], v[1]);
+  a.y = pack_bf16x2(v[2], v[3]);
+  a.z = pack_bf16x2(v[4], v[5]);
+  a.w = pack_bf16x2(v[6], v[7]);
+  b.x = pack_bf16x2(v[8], v[9]);
+  b.y = pack_bf16x2(v[10], v[11]);
+  b.z = pack_bf16x2(v[12], v[13]);
+  b.w = pack_bf16x2(v[14], v[15]);
+  const int u0 = 2 * group, u1 = 2 * group + 1;
+  *reinterpret_cast<uint4*>(slot + row * 128 + ((u0 ^ (row & 7)) << 4)) = a;
+  *reinterpret_cast<uint4*>(slot + row * 128 + ((u1 ^ (row & 7)) << 4)) = b;
+}
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* smem_src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 template <int EPI>
 __device__ __forceinline__ void epilogue16(const GemmParams& p, int m, int n, const uint32_t (&r)[16]) {
   const int valid = min(16, p.N - n);
-  if (valid <= 0) return;
+  if (valid <= 0 || p.ablate) return;
   float v[16];
 #pragma unroll
   for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
@@ -216,7 +357,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmA2a, const __grid_constant__ CUtensorMap tmA2b,
                 const __grid_constant__ CUtensorMap tmA2c, const __grid_constant__ CUtensorMap tmB2,
-                const GemmParams p) {
+                const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmOut2,
+                const __grid_constant__ CUtensorMap tmAux, const GemmParams p) {
   using C = Cfg<BN>;
   constexpr int S = C::kStages;
   constexpr uint32_t kIdesc = umma_idesc_bf16(BM, BN, A_MN, B_MN);
@@ -224,12 +366,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + S * C::kABytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + S * C::kBBytes);
+  uint8_t* sEpi = sB + S * C::kBBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + C::kEpiBytes);
   uint64_t* empty = full + S;
   uint64_t* acc_full = empty + S;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* aux_full = drain + 1;   // [4 warps][2 slots]: TMA load of the epilogue's second operand
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aux_full + 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id();
@@ -244,6 +388,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&acc_empty[b], 128);
     }
     mbar_init(drain, 1);
+    for (int i = 0; i < 8; ++i) mbar_init(&aux_full[i], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -400,6 +545,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = quarter * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
+    int store_idx = 0;
+    uint32_t aux_phase[2] = {0u, 0u};
     for (int work = blockIdx.x; work < total_work; work += gridDim.x) {
       int m_blk, n_blk, ks;
       tile_coords(p, work, m_blk, n_blk, ks);
@@ -411,6 +558,80 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int m = m_blk * BM + row;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      if constexpr (EPI != kEpiF32Acc) {
+        if (p.tma_store) {
+          // Each warp stages its 32 rows x 64 columns in smem and stores them
+          // with one TMA tensor store (full 128-byte lines; the per-row 16-byte
+          // stores of the fallback cost up to a third of the GEMM time).
+          uint8_t* wbuf = sEpi + quarter * (2 * C::kEpiSlotBytes);
+#pragma unroll 1
+          for (int c = 0; c < BN; c += 64) {
+            uint32_t r[4][16];
+#pragma unroll
+            for (int g = 0; g < 4; ++g) tmem_ld16(t_row + c + 16 * g, r[g]);
+            tmem_ld_wait();
+            // the slot(s) written below must no longer be read by an earlier store
+            if (lane == 0) {
+              if (EPI == kEpiGelu) {
+                bulk_wait_read<0>();
+              } else if (store_idx >= 2) {
+                bulk_wait_read<1>();
+              }
+            }
+            __syncwarp();
+            const int si = EPI == kEpiGelu ? 0 : (store_idx & 1);
+            uint8_t* slot = wbuf + si * C::kEpiSlotBytes;
+            uint8_t* slot2 = wbuf + C::kEpiSlotBytes;
+            const int n = n_blk * BN + c;
+            constexpr bool kAux = EPI == kEpiGatedRes || EPI == kEpiGeluBwd;
+            if constexpr (kAux) {
+              // the residual / GELU input tile arrives by TMA into the slot the
+              // output then overwrites (coalesced 128-byte lines both ways)
+              uint64_t* bar = &aux_full[quarter * 2 + si];
+              if (lane == 0) {
+                mbar_arrive_expect_tx(bar, C::kEpiSlotBytes);
+                tma_load_2d(slot, &tmAux, bar, n, m_blk * BM + quarter * 32);
+              }
+              if (!mbar_wait(bar, aux_phase[si], limit, abort_flag)) {
+                if (lane == 0) report_status(p.status, kStatusTimeoutAccFull, work);
+                *abort_flag = 1;
+              }
+              aux_phase[si] ^= 1u;
+            }
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+              float v[16], gv[16];
+              if (m < p.M && !p.ablate) {
+                if constexpr (kAux) {
+                  float a[16];
+                  unstage16(slot, lane, g, a);
+                  epilogue_vals<EPI>(p, m, n + 16 * g, r[g], v, gv, a);
+                } else {
+                  epilogue_vals<EPI>(p, m, n + 16 * g, r[g], v, gv);
+                }
+              } else {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] = gv[j] = 0.0f;
+              }
+              stage16(slot, lane, g, v);
+              if (EPI == kEpiGelu) stage16(slot2, lane, g, gv);
+            }
+            fence_async_smem_cta();
+            __syncwarp();
+            if (lane == 0 && !p.ablate) {
+              const int y = m_blk * BM + quarter * 32;
+              tma_store_2d(&tmOut, slot, n, y);
+              if (EPI == kEpiGelu) tma_store_2d(&tmOut2, slot2, n, y);
+            }
+            store_idx += EPI == kEpiGelu ? 2 : 1;
+          }
+          tc_fence_before();
+          mbar_arrive(&acc_empty[acc]);
+          acc ^= 1;
+          if (acc == 0) acc_phase ^= 1u;
+          continue;
+        }
+      }
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         uint32_t r0[16], r1[16];
@@ -428,6 +649,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
+    if (lane == 0 && store_idx > 0) bulk_wait_all();   // the TMA stores are complete before exit
   }
 
   tc_fence_before();
@@ -481,8 +703,8 @@ int num_sms(int device) {
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
 void launch_variant(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& a2a, const CUtensorMap& a2b,
-                    const CUtensorMap& a2c, const CUtensorMap& b2, const GemmParams& p, int device,
-                    cudaStream_t stream) {
+                    const CUtensorMap& a2c, const CUtensorMap& b2, const CUtensorMap& o1, const CUtensorMap& o2,
+                    const CUtensorMap& aux, const GemmParams& p, int device, cudaStream_t stream) {
   auto kernel = gemm_kernel<BN, A_MN, B_MN, EPI>;
   static bool configured[64] = {false};
   if (!configured[device]) {
@@ -491,7 +713,7 @@ void launch_variant(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMa
   }
   const int work = p.tiles_m * p.tiles_n * p.splits;
   const int grid = std::min(work, num_sms(device));
-  kernel<<<grid, kThreads, Cfg<BN>::kSmem, stream>>>(a, b, a2a, a2b, a2c, b2, p);
+  kernel<<<grid, kThreads, Cfg<BN>::kSmem, stream>>>(a, b, a2a, a2b, a2c, b2, o1, o2, aux, p);
   g_launches.fetch_add(1, std::memory_order_relaxed);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -598,6 +820,11 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, int64_
   p.pre = pre.has_value() ? reinterpret_cast<const __nv_bfloat16*>(pre->data_ptr()) : nullptr;
   p.ldp = pre.has_value() ? pre->stride(0) : 0;
   p.alpha = static_cast<float>(alpha);
+  static const int ablate = [] {
+    const char* v = std::getenv("H3_GEMM_ABLATE");
+    return v != nullptr ? std::atoi(v) : 0;
+  }();
+  p.ablate = ablate;
   p.status.word = status.data_ptr<int>();
   p.status.limit_ns = static_cast<uint64_t>(limit_ns);
 
@@ -607,13 +834,36 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, int64_
     TORCH_CHECK(out.scalar_type() == at::kBFloat16, "bf16 epilogues need a bf16 out");
   }
   if (epi == kEpiGatedRes) TORCH_CHECK(res.has_value() && gate.has_value(), "gated residual needs res and gate");
-  if (epi == kEpiRope) TORCH_CHECK(cos_t.has_value() && sin_t.has_value() && head_dim % 16 == 0, "rope tables");
+  if (epi == kEpiRope) {
+    TORCH_CHECK(cos_t.has_value() && sin_t.has_value() && head_dim % 16 == 0, "rope tables");
+    // the epilogue reads 8 consecutive entries of a row with float4 loads
+    TORCH_CHECK(cos_t->is_contiguous() && sin_t->is_contiguous() && cos_t->size(-1) == head_dim / 2 &&
+                    (reinterpret_cast<uintptr_t>(cos_t->data_ptr()) & 15u) == 0 &&
+                    (reinterpret_cast<uintptr_t>(sin_t->data_ptr()) & 15u) == 0,
+                "rope tables must be contiguous [T, head_dim/2] fp32 with 16-byte aligned rows");
+  }
   if (epi == kEpiGelu) TORCH_CHECK(out2.has_value(), "gelu epilogue needs out2");
   if (epi == kEpiGeluBwd) TORCH_CHECK(pre.has_value(), "gelu backward epilogue needs pre");
+  // bf16 outputs go out by TMA tensor stores when their layout allows a tensor map
+  CUtensorMap mo = ma, mo2 = ma;
+  auto storable = [&](const at::Tensor& t) {
+    return (reinterpret_cast<uintptr_t>(t.data_ptr()) & 15u) == 0 && (t.stride(0) * 2) % 16 == 0 && N >= 8 &&
+           t.stride(1) == 1;
+  };
+  p.tma_store = 0;
+  CUtensorMap maux = ma;
+  const at::Tensor* aux_t = epi == kEpiGatedRes ? &*res : (epi == kEpiGeluBwd ? &*pre : nullptr);
+  if (epi != kEpiF32Acc && storable(out) && (!out2.has_value() || storable(*out2)) &&
+      (aux_t == nullptr || (aux_t->scalar_type() == at::kBFloat16 && storable(*aux_t)))) {
+    mo = make_map(out.data_ptr(), M, N, out.stride(0), 32);
+    if (out2.has_value()) mo2 = make_map(out2->data_ptr(), M, N, out2->stride(0), 32);
+    if (aux_t != nullptr) maux = make_map(aux_t->data_ptr(), M, N, aux_t->stride(0), 32);
+    p.tma_store = 1;
+  }
 
 #define H3_GEMM_CASE(BN_, AMN_, BMN_, EPI_)                                                   \
   if (bn == BN_ && a_mn == AMN_ && b_mn == BMN_ && epi == EPI_) {                             \
-    launch_variant<BN_, AMN_, BMN_, EPI_>(ma, mb, ma2[0], ma2[1], ma2[2], mb2, p, device, stream); \
+    launch_variant<BN_, AMN_, BMN_, EPI_>(ma, mb, ma2[0], ma2[1], ma2[2], mb2, mo, mo2, maux, p, device, stream); \
     return;                                                                                   \
   }
   H3_GEMM_CASE(256, false, false, kEpiBf16)
