@@ -40,6 +40,20 @@ def test_gemm_plain_and_bias(K):
     K.check_status()
 
 
+def test_gemm_row_store_fallback(K):
+    """An output whose row stride is not a multiple of 16 bytes cannot have a
+    TMA tensor map: the epilogue falls back to per-row stores."""
+    from h3_a100.ops.native import EPI_BF16
+
+    torch.manual_seed(4)
+    x, w, b = bf(200, 256), bf(264, 256, scale=0.05), bf(264)
+    storage = torch.empty(200, 265, dtype=torch.bfloat16, device="cuda")   # 530-byte rows
+    out = storage[:, :264]
+    K._gemm(x, False, w, False, 200, 264, 256, EPI_BF16, out, bias=b, block_n=128)
+    close(out, R.linear(x.float(), w.float(), b.float()))
+    K.check_status()
+
+
 def test_gemm_large_tiles(K):
     torch.manual_seed(1)
     x, w = bf(1000, 1024), bf(1536, 1024, scale=0.03)
