@@ -93,15 +93,6 @@ __device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
   return d;
 }
 
-// Two exponentials in one MUFU instruction: 2^x for a pair of bf16 inputs,
-// bf16 results (the P operand is bf16 anyway; the inputs carry bf16
-// precision, 2^-8 relative, so P picks up at most ~|x|*2^-9 relative error).
-__device__ __forceinline__ uint32_t ex2_bf16x2(uint32_t x2) {
-  uint32_t y;
-  asm("ex2.approx.ftz.bf16x2 %0, %1;" : "=r"(y) : "r"(x2));
-  return y;
-}
-
 // 2^x on the FMA pipe, to take part of the exponentials off the MUFU unit:
 // x = n + f with n = round(x) (magic-number add, no conversion instruction)
 // and f in [-1/2, 1/2]; 2^f is a cubic least-squares fit at Chebyshev nodes
@@ -191,35 +182,6 @@ __device__ __forceinline__ float row_max(const uint32_t (&r)[kBKV / 32][32]) {
 // every 8 pairs go through the FMA-pipe exponential, the rest to MUFU: MUFU
 // takes 8 cycles per warp instruction, so at POLY = 0 the exponentials alone
 // are ~1,024 cycles per KV tile and warp, on the softmax's critical path.
-// Same with the exponentials as packed bf16x2 MUFU operations: half the
-// MUFU issue, and P comes out already packed; the row sum adds the bf16 P
-// values (the weights the PV MMA actually uses).  Masked keys hold -inf, so
-// their P is exactly 0.
-__device__ __forceinline__ float row_exp_pack_bf16(uint32_t tS, const uint32_t (&r)[kBKV / 32][32], float scale,
-                                                   float m) {
-  const uint64_t scale2 = pack2(scale, scale), negm2 = pack2(-m, -m);
-  uint64_t acc[4];
-#pragma unroll
-  for (int k = 0; k < 4; ++k) acc[k] = 0ull;
-#pragma unroll
-  for (int c = 0; c < kBKV / 32; ++c) {
-    uint32_t packed[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      float xa, xb;
-      unpack2(fma2(pack2(__uint_as_float(r[c][2 * i]), __uint_as_float(r[c][2 * i + 1])), scale2, negm2), xa, xb);
-      const uint32_t pv = ex2_bf16x2(pack_bf16x2(xa, xb));
-      packed[i] = pv;
-      acc[i & 3] = add2(acc[i & 3], pack2(__uint_as_float(pv << 16), __uint_as_float(pv & 0xffff0000u)));
-    }
-    tmem_st16(tS + c * 16, packed);
-  }
-  const uint64_t s2 = add2(add2(acc[0], acc[1]), add2(acc[2], acc[3]));
-  float sa, sb;
-  unpack2(s2, sa, sb);
-  return sa + sb;
-}
-
 template <bool MASKED, int POLY>
 __device__ __forceinline__ float row_exp_pack(uint32_t tS, const uint32_t (&r)[kBKV / 32][32], int valid, float scale,
                                               float m) {
@@ -468,13 +430,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     }
     tc_fence_after();
     // P = 2^(s*scale - m) as packed bf16 pairs over the consumed S columns.
-    float rowsum;
-    if constexpr (POLY < 0) {
-      rowsum = row_exp_pack_bf16(tS, r, p.scale_log2, m_used);
-    } else {
-      rowsum = kv_valid >= kBKV ? row_exp_pack<false, (POLY > 0 ? POLY : 0)>(tS, r, kv_valid, p.scale_log2, m_used)
-                                : row_exp_pack<true, (POLY > 0 ? POLY : 0)>(tS, r, kv_valid, p.scale_log2, m_used);
-    }
+    const float rowsum = kv_valid >= kBKV ? row_exp_pack<false, POLY>(tS, r, kv_valid, p.scale_log2, m_used)
+                                          : row_exp_pack<true, POLY>(tS, r, kv_valid, p.scale_log2, m_used);
     l += rowsum;
     // Rescale O_t after P is written (the S registers are dead by then, so
     // the O chunk does not push the row past the register budget); PV_t(j)
@@ -555,7 +512,7 @@ std::vector<at::Tensor> attention_fwd(const at::Tensor& qkv, int64_t heads, int6
   static bool configured[64] = {false};
   const int device = qkv.get_device();
   if (!configured[device]) {
-    for (auto fn : {attn_fwd_kernel<0>, attn_fwd_kernel<4>, attn_fwd_kernel<-1>}) {
+    for (auto fn : {attn_fwd_kernel<0>, attn_fwd_kernel<4>}) {
       cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
       // setmaxnreg.inc waits until the producer warpgroup has released enough
       // registers; that only balances if the launch count is the assumed one.
@@ -566,8 +523,9 @@ std::vector<at::Tensor> attention_fwd(const at::Tensor& qkv, int64_t heads, int6
     }
     configured[device] = true;
   }
-  // Exponentials: 0 = fp32 MUFU, 4 = four of every 8 pairs on the FMA pipe,
-  // -1 = packed bf16x2 MUFU.  H3_ATTN_FWD_POLY selects it for measurements only.
+  // Exponentials: 0 = MUFU only, 4 = four of every 8 pairs on the FMA pipe
+  // (measured slower at this issue rate; so was a packed bf16x2 MUFU form).
+  // H3_ATTN_FWD_POLY selects it for measurements only.
   static const int poly = [] {
     const char* v = std::getenv("H3_ATTN_FWD_POLY");
     return v != nullptr ? std::atoi(v) : 0;
@@ -575,7 +533,6 @@ std::vector<at::Tensor> attention_fwd(const at::Tensor& qkv, int64_t heads, int6
   dim3 grid(static_cast<unsigned>((T + kQTiles * kBQ - 1) / (kQTiles * kBQ)), static_cast<unsigned>(heads));
   cudaStream_t stream = at::cuda::getCurrentCUDAStream(device).stream();
   switch (poly) {
-    case -1: attn_fwd_kernel<-1><<<grid, kThreads, kSmem, stream>>>(tm, p); break;
     case 4: attn_fwd_kernel<4><<<grid, kThreads, kSmem, stream>>>(tm, p); break;
     default: attn_fwd_kernel<0><<<grid, kThreads, kSmem, stream>>>(tm, p); break;
   }
