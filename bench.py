@@ -138,11 +138,20 @@ def main() -> None:
     launches = int(pdist.all_reduce_max(launches))
     h2d_per_step = (trainer.h2d_bytes - h2d0) / max(1, args.steps)
     s_per_cycle = dev_ms / 1000.0 / args.steps
-    headline = args.num_blocks is None
+    from h3_a100.config import get as cfg_get
+    from h3_a100.models.shared_backbone import sequence_tokens
+
+    dmd = cfg_get(config, "training.dmd", {}) or {}
+    canvas = f"{dmd.get('height', 768)}x{dmd.get('width', 1344)}x{dmd.get('num_frames', 124)}f"
+    # only the full 50-block model on the 768x1344x124 canvas is the published metric's config
+    headline = args.num_blocks is None and canvas == "768x1344x124f"
     if rank == 0:
-        tokens = 31 * 24 * 42 + 512 + 5970
+        tokens = sequence_tokens(config)
+        metric = METRIC if canvas == "768x1344x124f" else METRIC.replace("768x1344x124f", canvas)
+        counts = model_cfg.param_counts()
+        lora_params = trainer.model.lora["student"].numel()
         line = {
-            "metric": METRIC,
+            "metric": metric,
             "value": round(s_per_cycle, 4),
             "unit": "s/cycle",
             "n_gpus": world,
@@ -158,7 +167,8 @@ def main() -> None:
             "peak_gib_per_rank": round(peak_gib, 2),
             "config": {
                 "model": (f"H3-shaped DiT {model_cfg.num_blocks} blocks hidden {model_cfg.hidden} "
-                          f"ffn {model_cfg.ffn} (33.2B frozen + 2x691.8M LoRA r128)"),
+                          f"ffn {model_cfg.ffn} ({counts['frozen_total'] / 1e9:.1f}B frozen + "
+                          f"2x{lora_params / 1e6:.1f}M LoRA r128)"),
                 "global_batch": world,
                 "seq_len": tokens,
                 "parallelism": f"fsdp{world}" if world > 1 else "single",
