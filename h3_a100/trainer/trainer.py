@@ -250,6 +250,13 @@ class H3DmdTrainer(CheckpointMixin, LoopMixin, DMDRuntimeMixin):
         self.fake_trainable_params = model.role_parameters(FAKE)
         self._validate_shared_parameter_contract()
         world_comm = self.comm
+        if pdist.topology().replicate_size > 1:
+            # The adapters are replicated on every rank and every rank draws its
+            # own sample, so LoRA gradients average over the whole world (the
+            # shard group only spans one replica).
+            from ..parallel.comm import TorchComm
+
+            world_comm = TorchComm(None, self.device)
         for role, ocfg, total in ((STUDENT, self.student_optimizer_config, self.max_train_iters),
                                   (FAKE, self.fake_optimizer_config, self.max_train_iters * self.fake_update_ratio)):
             self.optimizers[role] = FlatAdamW(

@@ -57,11 +57,14 @@ def _run(fn, world: int, *args, timeout: float = 300.0):
     return msgs, [p.exitcode for p in procs]
 
 
-def _tiny_config(world: int, out_dir: str | None = None, **training):
+def _tiny_config(world: int, out_dir: str | None = None, shard_size: int | None = None, **training):
     from h3_a100.config import load_config
 
+    dist_cfg = {"fsdp2": {"size": shard_size or world}, "timeout_minutes": 2}
+    if shard_size is not None:
+        dist_cfg["hybrid_shard"] = {"enabled": True, "shard_size": shard_size}
     overrides = {
-        "distributed": {"fsdp2": {"size": world}, "timeout_minutes": 2},
+        "distributed": dist_cfg,
         "training": {"a100": {"matched_compute": {"expected_world_size": world}}, **training},
         "kernels": {"backend": "torch", "device": "cpu"},
     }
@@ -71,12 +74,12 @@ def _tiny_config(world: int, out_dir: str | None = None, **training):
 
 
 # --------------------------------------------------------------------------- matched cycle at world N
-def _cycle_rank(rank, world, port, queue, iters):
+def _cycle_rank(rank, world, port, queue, iters, shard_size=None):
     try:
         _env(rank, world, port)
         from h3_a100.api import build_trainer
 
-        trainer = build_trainer(_tiny_config(world, max_train_iters=iters))
+        trainer = build_trainer(_tiny_config(world, shard_size=shard_size, max_train_iters=iters))
         trainer.setup()
         samples = trainer.samples()
         losses = [trainer.run_cycle(samples, i) for i in range(iters)]
@@ -94,9 +97,11 @@ def _cycle_rank(rank, world, port, queue, iters):
             dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_matched_cycle_gloo(world):
-    msgs, codes = _run(_cycle_rank, world, 2)
+@pytest.mark.parametrize("world,shard_size", [(2, None), (4, None), (4, 2)], ids=["world2", "world4", "hsdp2x2"])
+def test_matched_cycle_gloo(world, shard_size):
+    """Full shard at world 2 and 4, and HSDP (2 replicas x 2 shards): the
+    adapters stay identical on every rank of the world."""
+    msgs, codes = _run(_cycle_rank, world, 2, shard_size)
     errors = [m for m in msgs if m[0] == "error"]
     assert not errors, "\n".join(m[2] for m in errors)
     assert codes == [0] * world
