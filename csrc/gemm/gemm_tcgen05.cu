@@ -40,7 +40,9 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int kThreads = 192;
+constexpr int kThreads = 256;   // TMA, MMA, 4 epilogue warps, 2 gather warps
+constexpr int kGatherThreads = 64;
+constexpr int kMaxPeers = 8;
 
 struct GemmParams {
   int M, N;
@@ -66,6 +68,19 @@ struct GemmParams {
   long ldp;
   float alpha;
   int tma_store;  // bf16 outputs leave through smem + TMA tensor stores (full 128-byte lines)
+  // Fused all-gather of B (K-major): rank r owns rows [r*g_rows, (r+1)*g_rows) of
+  // the [N, K] weight in its own memory (g_src[r], a peer pointer); the gather
+  // warps copy each N-tile's rows into the local B buffer (the tmB base, g_dst)
+  // and raise g_flags[tile] = g_epoch; the producer waits for the flag before
+  // TMA-loading the tile, so the transfer overlaps the GEMM tile by tile.
+  int gather;
+  int g_world;
+  long g_rows;
+  long g_row_bytes;
+  const uint8_t* g_src[kMaxPeers];
+  uint8_t* g_dst;
+  int* g_flags;
+  int g_epoch;
   int ablate;     // diagnostic only (H3_GEMM_ABLATE): 1 = skip the epilogue's global stores
   KernelStatus status;
 };
@@ -230,6 +245,29 @@ __device__ __forceinline__ void epilogue_vals(const GemmParams& p, int m, int n,
 #pragma unroll
     for (int j = 0; j < 16; ++j) v[j] = bf16_round(v[j]) * gelu_tanh_grad_f(pre[j]);
   }
+}
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_gpu(int* p, int v) {
+  asm volatile("st.release.gpu.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Generic-proxy global writes (the gather warps' stores) become visible to the
+// async proxy (TMA loads) issued after this.
+__device__ __forceinline__ void fence_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
+// Bounded wait for a gathered N-tile (time limit and an iteration cap).
+__device__ __forceinline__ bool wait_tile_flag(const int* flag, int epoch, uint64_t limit_ns, volatile int* abort) {
+  if (ld_acquire_gpu(flag) == epoch) return true;
+  const uint64_t start = global_timer_ns();
+  for (uint32_t it = 1; it != 0u; ++it) {
+    if (ld_acquire_gpu(flag) == epoch) return true;
+    if ((it & 63u) == 0u && (*abort || global_timer_ns() - start > limit_ns)) return false;
+  }
+  return false;
 }
 
 __device__ __forceinline__ void fence_async_smem_cta() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
@@ -431,6 +469,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int sec = n0 / p.section_n;
           a2 = sec == 0 ? &tmA2a : (sec == 1 ? &tmA2b : &tmA2c);
         }
+        if (p.gather) {
+          if (!wait_tile_flag(p.g_flags + n_blk, p.g_epoch, limit, abort_flag)) {
+            report_status(p.status, kStatusTimeoutPeer, n_blk);
+            *abort_flag = 1;
+            break;
+          }
+          fence_async_global();
+        }
         for (int kb = kb_lo; kb < kb_hi; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, limit, abort_flag)) {
             report_status(p.status, kStatusTimeoutEmpty, kb);
@@ -478,6 +524,41 @@ __global__ void __launch_bounds__(kThreads, 1)
           // Abort path: wait again without the abort short-cut, still bounded.
           volatile int never = 0;
           mbar_wait(&full[s], issued_phase[s], limit, &never);
+        }
+      }
+    }
+  } else if (warp >= 6) {
+    // ------------------------------------------------------------ gather warps
+    if (p.gather) {
+      const int gt = threadIdx.x - 6 * 32;   // 0 .. kGatherThreads-1
+      const long units_per_row = p.g_row_bytes >> 4;
+      for (int nt = blockIdx.x; nt < p.tiles_n && !*abort_flag; nt += gridDim.x) {
+        const long r0 = static_cast<long>(nt) * BN;
+        const long r1 = min(static_cast<long>(p.N), r0 + BN);
+        const long units = (r1 - r0) * units_per_row;
+        constexpr int kU = 4;
+        for (long base = gt; base < units; base += kGatherThreads * kU) {
+          uint4 v[kU];
+#pragma unroll
+          for (int k = 0; k < kU; ++k) {
+            const long u = base + k * kGatherThreads;
+            if (u < units) {
+              const long row = r0 + u / units_per_row;
+              const int owner = static_cast<int>(row / p.g_rows);
+              const long local = (row - owner * p.g_rows) * units_per_row + u % units_per_row;
+              v[k] = reinterpret_cast<const uint4*>(p.g_src[owner])[local];
+            }
+          }
+#pragma unroll
+          for (int k = 0; k < kU; ++k) {
+            const long u = base + k * kGatherThreads;
+            if (u < units) reinterpret_cast<uint4*>(p.g_dst)[r0 * units_per_row + u] = v[k];
+          }
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(kGatherThreads) : "memory");
+        if (gt == 0) {
+          __threadfence();
+          st_release_gpu(p.g_flags + nt, p.g_epoch);
         }
       }
     }
@@ -760,7 +841,8 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, int64_
           const c10::optional<at::Tensor>& gate, int64_t split_row, const c10::optional<at::Tensor>& cos_t,
           const c10::optional<at::Tensor>& sin_t, int64_t rope_cols, int64_t head_dim,
           const c10::optional<at::Tensor>& pre, double alpha, int64_t splits, int64_t block_n,
-          const at::Tensor& status, int64_t limit_ns) {
+          const at::Tensor& status, int64_t limit_ns, const std::vector<int64_t>& gather_src,
+          int64_t gather_rows, const c10::optional<at::Tensor>& gather_flags, int64_t gather_epoch) {
   const int device = A.get_device();
   c10::cuda::CUDAGuard guard(device);
   cudaStream_t stream = at::cuda::getCurrentCUDAStream(device).stream();
@@ -827,6 +909,27 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, int64_
   p.ablate = ablate;
   p.status.word = status.data_ptr<int>();
   p.status.limit_ns = static_cast<uint64_t>(limit_ns);
+  p.gather = 0;
+  if (!gather_src.empty()) {
+    // B is this rank's local gathered buffer; the rows come from the peers.
+    TORCH_CHECK(!b_mn && ob.ld == K && (K * 2) % 16 == 0, "fused all-gather needs a contiguous K-major B");
+    TORCH_CHECK(gather_src.size() <= static_cast<size_t>(kMaxPeers), "at most 8 peers");
+    TORCH_CHECK(gather_rows > 0 && gather_rows * static_cast<int64_t>(gather_src.size()) >= N, "row shards");
+    TORCH_CHECK(gather_flags.has_value() && gather_flags->scalar_type() == at::kInt &&
+                    gather_flags->numel() >= p.tiles_n, "one int32 flag per N-tile");
+    TORCH_CHECK(K2 == 0 && p.splits == 1, "fused all-gather supports the plain K-phase only");
+    p.gather = 1;
+    p.g_world = static_cast<int>(gather_src.size());
+    p.g_rows = gather_rows;
+    p.g_row_bytes = K * 2;
+    for (size_t i = 0; i < gather_src.size(); ++i) {
+      TORCH_CHECK((gather_src[i] & 15) == 0, "peer shards must be 16-byte aligned");
+      p.g_src[i] = reinterpret_cast<const uint8_t*>(gather_src[i]);
+    }
+    p.g_dst = reinterpret_cast<uint8_t*>(const_cast<void*>(ob.ptr));
+    p.g_flags = gather_flags->data_ptr<int>();
+    p.g_epoch = static_cast<int>(gather_epoch);
+  }
 
   if (epi == kEpiF32Acc) {
     TORCH_CHECK(out.scalar_type() == at::kFloat, "fp32 accumulate epilogue needs an fp32 out");

@@ -11,7 +11,10 @@ configs/h3_fused_collective_sweep.yaml`` times, on every rank with CUDA events
   the fused GEMV whose epilogue stores into every rank's output);
 * ``lora_step``: one role's optimizer step on the r128 LoRA of the config
   (NCCL reduce-scatter + norm all-reduce + AdamW + all-gather, vs the single
-  cooperative peer-memory kernel).
+  cooperative peer-memory kernel);
+* ``allgather_qkv_gemm``: the fused QKV GEMM on a weight sharded by rows across
+  the ranks (NCCL all-gather then the GEMM, vs the GEMM whose gather warps pull
+  each N-tile from its owner while earlier tiles are multiplied).
 
 Each line carries the path's roofline: the slower of its HBM bytes at the
 measured copy bandwidth and its NVLink bytes per GPU at 770 GB/s per direction
@@ -168,7 +171,42 @@ def main(argv=None) -> None:
         if impl == "p2p":
             comm.check_status()
         K.check_status()
-        del shard, flat, grad, opt
+
+        # ---- QKV GEMM on a row-sharded weight: all-gather then GEMM (NCCL) vs
+        # the GEMM whose gather warps pull each N-tile from its owner (p2p)
+        from .models.shared_backbone import sequence_tokens
+
+        m_tok = sequence_tokens(load_config(args.config))
+        n_q, k_q = 3 * h, h
+        rows_q = n_q // world
+        x_q = (torch.randn(m_tok, k_q, device=dev) * 0.5).to(torch.bfloat16)
+        w_shard = comm.alloc_shard(rows_q * k_q, torch.bfloat16).view(rows_q, k_q)
+        w_shard.normal_(0, 0.02)
+        w_full = torch.empty(n_q, k_q, dtype=torch.bfloat16, device=dev)
+        torch.cuda.synchronize()
+        dist.barrier()
+        if impl == "p2p":
+            flags = torch.zeros((n_q + 255) // 256, dtype=torch.int32, device=dev)
+
+            def ag_gemm():
+                K.linear_allgather(x_q, w_full, comm.gather_spec(w_shard, rows_q, flags))
+        else:
+            def ag_gemm():
+                dist.all_gather_into_tensor(w_full, w_shard)
+                K.linear(x_q, w_full)
+
+        ms = _time(ag_gemm, max(5, args.iters // 2))
+        flops = 2.0 * m_tok * n_q * k_q
+        link = n_q * k_q * 2 * (world - 1) / world
+        roof_ms = max(flops / (float(peaks.get("bf16_tflops", 1590.0)) * 1e12), link / (NVLINK_GBS * 1e9)) * 1e3
+        lines.append({"op": "allgather_qkv_gemm", "impl": impl, "n_gpus": world, "ms": round(ms, 4),
+                      "roofline_ms": round(roof_ms, 4), "frac_of_roofline": round(roof_ms / ms, 3),
+                      "tflops": round(flops / ms / 1e9, 1), "m": m_tok, "n": n_q, "k": k_q,
+                      "nvlink_bytes_per_gpu": int(link)})
+        K.check_status()
+        if impl == "p2p":
+            comm.check_status()
+        del shard, flat, grad, opt, w_shard, w_full, x_q
         torch.cuda.synchronize()
         dist.barrier()
 

@@ -73,10 +73,14 @@ class NativeKernels:
 
     def _gemm(self, A, a_mn, B, b_mn, M, N, K, epi, out, *, A2=(), B2=None, K2=0, section_n=0, out2=None,
               bias=None, res=None, gate=None, split_row=0, cos=None, sin=None, rope_cols=0, head_dim=0,
-              pre=None, alpha=1.0, splits=1, block_n=256):
+              pre=None, alpha=1.0, splits=1, block_n=256, gather=None):
+        """``gather`` = (peer shard pointers, rows per rank, int32 tile flags, epoch) fuses the
+        all-gather of a row-sharded K-major B into the GEMM (B is then the local destination)."""
+        g_src, g_rows, g_flags, g_epoch = gather if gather is not None else ([], 0, None, 0)
         self.C.gemm(A, a_mn, B, b_mn, int(M), int(N), int(K), list(A2), B2, int(K2), int(section_n), int(epi),
                     out, out2, bias, res, gate, int(split_row), cos, sin, int(rope_cols), int(head_dim), pre,
-                    float(alpha), int(splits), int(block_n), self.status, self.limit_ns)
+                    float(alpha), int(splits), int(block_n), self.status, self.limit_ns, list(g_src), int(g_rows),
+                    g_flags, int(g_epoch))
 
     def _splits(self, tiles: int, k: int) -> int:
         kb = (k + 63) // 64
@@ -197,6 +201,18 @@ class NativeKernels:
                    weight_decay, step, max_norm):
         self.C.adamw_step(master, exp_avg, exp_avg_sq, grad, param_out, norm, lr, beta1, beta2, eps,
                           weight_decay, int(step), max_norm)
+
+    def linear_allgather(self, x, w_local, gather, bias=None, block_n=256):
+        """y = x W^T + b where W's rows live sharded on the peers: the GEMM's
+        gather warps pull each N-tile's rows into ``w_local`` (this rank's
+        full-size buffer) while the tensor core works on the tiles already
+        there.  ``gather`` comes from ``PeerComm.gather_spec``."""
+        m, k = x.shape
+        n = w_local.shape[0]
+        out = torch.empty(m, n, dtype=torch.bfloat16, device=x.device)
+        self._gemm(x.contiguous(), False, w_local, False, m, n, k, EPI_BF16, out, bias=bias, block_n=block_n,
+                   gather=gather)
+        return out
 
     # ------------------------------------------------------------ flow / DMD
     def flow_step(self, xt, velocity, sigma, sigma_next, out_dtype):

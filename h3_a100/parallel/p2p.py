@@ -129,6 +129,14 @@ class PeerComm(TorchComm):
         self.bytes_peer += (self.world_size - 1) * shard.numel() * shard.element_size()
         return _Pending(out, event)
 
+    # ---------------------------------------------------------------- all-gather fused into a GEMM
+    def gather_spec(self, shard: torch.Tensor, rows_per_rank: int, flags: torch.Tensor):
+        """Arguments for ``NativeKernels.linear_allgather``: every rank's shard
+        of a row-sharded weight (symmetric buffer of ``rows_per_rank`` rows),
+        this rank's per-N-tile flags (zeroed int32, reused across calls) and a
+        fresh epoch.  No barrier is needed: the shards are written once."""
+        return self.peer_ptrs(shard), int(rows_per_rank), flags, self.next_epoch()
+
     # ---------------------------------------------------------------- AdaLN GEMV + all-gather
     def adaln_project(self, temb: torch.Tensor, w_rows: torch.Tensor, b_rows: torch.Tensor,
                       out: torch.Tensor) -> torch.Tensor:

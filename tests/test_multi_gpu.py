@@ -107,6 +107,27 @@ def _collectives(rank: int, port: int, errors, multimem: str = "0") -> None:
             ref_opt.step(1e-2)
             err = (flat.float() - ref_store.flat.float()).abs().max().item()
             assert err < 2e-2, f"fused LoRA step mismatch {err} at step {step}"
+        # 4. weight all-gather fused into the GEMM (row-sharded W, tile flags)
+        n, k, m = 1024, 512, 700
+        rows = n // WORLD
+        gw = torch.Generator(device=dev).manual_seed(5)
+        w_full = (torch.randn(n, k, device=dev, generator=gw) * 0.05).to(torch.bfloat16)
+        bias = torch.randn(n, device=dev, generator=gw).to(torch.bfloat16)
+        x = torch.randn(m, k, device=dev, generator=torch.Generator(device=dev).manual_seed(6 + rank)).to(torch.bfloat16)
+        w_shard = comm.alloc_symmetric(rows * k, torch.bfloat16).view(rows, k)
+        w_shard.copy_(w_full[rank * rows:(rank + 1) * rows])
+        torch.cuda.synchronize()
+        dist.barrier()
+        w_local = torch.empty(n, k, dtype=torch.bfloat16, device=dev)
+        flags = torch.zeros((n + 255) // 256, dtype=torch.int32, device=dev)
+        ref = K.linear(x, w_full, bias)
+        for _ in range(2):   # the second call reuses the flags with a new epoch
+            w_local.zero_()
+            y = K.linear_allgather(x, w_local, comm.gather_spec(w_shard, rows, flags), bias=bias)
+            torch.cuda.synchronize()
+            K.check_status()
+            assert torch.equal(w_local, w_full), "gathered weight differs"
+            assert torch.equal(y, ref), "fused all-gather GEMM differs from the GEMM on the full weight"
         dist.barrier()
     except Exception:  # noqa: BLE001 - reported to the parent
         errors.put(f"rank {rank}: {traceback.format_exc()}")

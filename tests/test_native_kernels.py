@@ -54,6 +54,28 @@ def test_gemm_row_store_fallback(K):
     K.check_status()
 
 
+def test_gemm_fused_gather_local_owners(K):
+    """The all-gather fused into the GEMM, on one GPU: the weight's rows are
+    split over three 'owner' buffers in local memory (the peer case differs
+    only in where those pointers point); the gathered weight and the product
+    must equal the plain GEMM on the full weight, on two calls in a row."""
+    torch.manual_seed(5)
+    n, k, m = 1000, 512, 300
+    rows = 334                                      # owners hold 334, 334, 332 rows
+    w, b = bf(n, k, scale=0.05), bf(n)
+    x = bf(m, k)
+    shards = [w[i * rows:(i + 1) * rows].clone() for i in range(3)]
+    flags = torch.zeros((n + 255) // 256, dtype=torch.int32, device="cuda")
+    ref = K.linear(x, w, b)
+    for epoch in (1, 2):
+        w_local = torch.zeros_like(w)
+        y = K.linear_allgather(x, w_local, ([t.data_ptr() for t in shards], rows, flags, epoch), bias=b)
+        torch.cuda.synchronize()
+        K.check_status()
+        assert torch.equal(w_local, w)
+        assert torch.equal(y, ref)
+
+
 def test_gemm_large_tiles(K):
     torch.manual_seed(1)
     x, w = bf(1000, 1024), bf(1536, 1024, scale=0.03)
