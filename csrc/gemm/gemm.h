@@ -23,7 +23,7 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, int64_
           const c10::optional<at::Tensor>& sin_t, int64_t rope_cols, int64_t head_dim,
           const c10::optional<at::Tensor>& pre, double alpha, int64_t splits, int64_t block_n,
           const at::Tensor& status, int64_t limit_ns, const std::vector<int64_t>& gather_src,
-          int64_t gather_rows, const c10::optional<at::Tensor>& gather_flags, int64_t gather_epoch);
+          int64_t gather_rows, const c10::optional<at::Tensor>& gather_flags);
 
 uint64_t launch_count();
 void note_launch();

@@ -69,10 +69,12 @@ struct GemmParams {
   float alpha;
   int tma_store;  // bf16 outputs leave through smem + TMA tensor stores (full 128-byte lines)
   // Fused all-gather of B (K-major): rank r owns rows [r*g_rows, (r+1)*g_rows) of
-  // the [N, K] weight in its own memory (g_src[r], a peer pointer); the gather
-  // warps copy each N-tile's rows into the local B buffer (the tmB base, g_dst)
-  // and raise g_flags[tile] = g_epoch; the producer waits for the flag before
-  // TMA-loading the tile, so the transfer overlaps the GEMM tile by tile.
+  // the [N, K] weight in its own memory (g_src[r], a peer pointer).  Every
+  // CTA's gather warps copy a 1/gridDim slice of each N-tile (in tile order)
+  // into the local B buffer (the tmB base, g_dst) and count it in
+  // g_flags[tile] (zeroed before the launch); a producer waits until all
+  // gridDim slices of its tile have landed before TMA-loading it, so the
+  // transfer overlaps the GEMM tile by tile.
   int gather;
   int g_world;
   long g_rows;
@@ -80,7 +82,6 @@ struct GemmParams {
   const uint8_t* g_src[kMaxPeers];
   uint8_t* g_dst;
   int* g_flags;
-  int g_epoch;
   int ablate;     // diagnostic only (H3_GEMM_ABLATE): 1 = skip the epilogue's global stores
   KernelStatus status;
 };
@@ -252,19 +253,19 @@ __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
   asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ void st_release_gpu(int* p, int v) {
-  asm volatile("st.release.gpu.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void red_release_add_gpu(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 // Generic-proxy global writes (the gather warps' stores) become visible to the
 // async proxy (TMA loads) issued after this.
 __device__ __forceinline__ void fence_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 
-// Bounded wait for a gathered N-tile (time limit and an iteration cap).
-__device__ __forceinline__ bool wait_tile_flag(const int* flag, int epoch, uint64_t limit_ns, volatile int* abort) {
-  if (ld_acquire_gpu(flag) == epoch) return true;
+// Bounded wait until `target` slices of a gathered N-tile have landed.
+__device__ __forceinline__ bool wait_tile_flag(const int* flag, int target, uint64_t limit_ns, volatile int* abort) {
+  if (ld_acquire_gpu(flag) >= target) return true;
   const uint64_t start = global_timer_ns();
   for (uint32_t it = 1; it != 0u; ++it) {
-    if (ld_acquire_gpu(flag) == epoch) return true;
+    if (ld_acquire_gpu(flag) >= target) return true;
     if ((it & 63u) == 0u && (*abort || global_timer_ns() - start > limit_ns)) return false;
   }
   return false;
@@ -470,7 +471,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           a2 = sec == 0 ? &tmA2a : (sec == 1 ? &tmA2b : &tmA2c);
         }
         if (p.gather) {
-          if (!wait_tile_flag(p.g_flags + n_blk, p.g_epoch, limit, abort_flag)) {
+          if (!wait_tile_flag(p.g_flags + n_blk, static_cast<int>(gridDim.x), limit, abort_flag)) {
             report_status(p.status, kStatusTimeoutPeer, n_blk);
             *abort_flag = 1;
             break;
@@ -532,17 +533,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (p.gather) {
       const int gt = threadIdx.x - 6 * 32;   // 0 .. kGatherThreads-1
       const long units_per_row = p.g_row_bytes >> 4;
-      for (int nt = blockIdx.x; nt < p.tiles_n && !*abort_flag; nt += gridDim.x) {
+      // Tiles in order (the producers need the low N-tiles first); every CTA
+      // copies its slice of each tile, so all SMs' bandwidth goes to tile 0 first.
+      for (int nt = 0; nt < p.tiles_n && !*abort_flag; ++nt) {
         const long r0 = static_cast<long>(nt) * BN;
         const long r1 = min(static_cast<long>(p.N), r0 + BN);
         const long units = (r1 - r0) * units_per_row;
+        const long per_cta = (units + gridDim.x - 1) / gridDim.x;
+        const long u_lo = min(units, blockIdx.x * per_cta), u_hi = min(units, u_lo + per_cta);
         constexpr int kU = 4;
-        for (long base = gt; base < units; base += kGatherThreads * kU) {
+        for (long base = u_lo + gt; base < u_hi; base += kGatherThreads * kU) {
           uint4 v[kU];
 #pragma unroll
           for (int k = 0; k < kU; ++k) {
             const long u = base + k * kGatherThreads;
-            if (u < units) {
+            if (u < u_hi) {
               const long row = r0 + u / units_per_row;
               const int owner = static_cast<int>(row / p.g_rows);
               const long local = (row - owner * p.g_rows) * units_per_row + u % units_per_row;
@@ -552,13 +557,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int k = 0; k < kU; ++k) {
             const long u = base + k * kGatherThreads;
-            if (u < units) reinterpret_cast<uint4*>(p.g_dst)[r0 * units_per_row + u] = v[k];
+            if (u < u_hi) reinterpret_cast<uint4*>(p.g_dst)[r0 * units_per_row + u] = v[k];
           }
         }
         asm volatile("bar.sync 1, %0;" ::"n"(kGatherThreads) : "memory");
         if (gt == 0) {
           __threadfence();
-          st_release_gpu(p.g_flags + nt, p.g_epoch);
+          red_release_add_gpu(p.g_flags + nt, 1);
         }
       }
     }
@@ -842,7 +847,7 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, int64_
           const c10::optional<at::Tensor>& sin_t, int64_t rope_cols, int64_t head_dim,
           const c10::optional<at::Tensor>& pre, double alpha, int64_t splits, int64_t block_n,
           const at::Tensor& status, int64_t limit_ns, const std::vector<int64_t>& gather_src,
-          int64_t gather_rows, const c10::optional<at::Tensor>& gather_flags, int64_t gather_epoch) {
+          int64_t gather_rows, const c10::optional<at::Tensor>& gather_flags) {
   const int device = A.get_device();
   c10::cuda::CUDAGuard guard(device);
   cudaStream_t stream = at::cuda::getCurrentCUDAStream(device).stream();
@@ -928,7 +933,8 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, int64_
     }
     p.g_dst = reinterpret_cast<uint8_t*>(const_cast<void*>(ob.ptr));
     p.g_flags = gather_flags->data_ptr<int>();
-    p.g_epoch = static_cast<int>(gather_epoch);
+    // slice counters start at zero every call (same stream, before the launch)
+    C10_CUDA_CHECK(cudaMemsetAsync(p.g_flags, 0, sizeof(int) * p.tiles_n, stream));
   }
 
   if (epi == kEpiF32Acc) {

@@ -74,13 +74,13 @@ class NativeKernels:
     def _gemm(self, A, a_mn, B, b_mn, M, N, K, epi, out, *, A2=(), B2=None, K2=0, section_n=0, out2=None,
               bias=None, res=None, gate=None, split_row=0, cos=None, sin=None, rope_cols=0, head_dim=0,
               pre=None, alpha=1.0, splits=1, block_n=256, gather=None):
-        """``gather`` = (peer shard pointers, rows per rank, int32 tile flags, epoch) fuses the
-        all-gather of a row-sharded K-major B into the GEMM (B is then the local destination)."""
-        g_src, g_rows, g_flags, g_epoch = gather if gather is not None else ([], 0, None, 0)
+        """``gather`` = (owner shard pointers, rows per owner, int32 per-N-tile counters) fuses
+        the all-gather of a row-sharded K-major B into the GEMM (B is then the local destination)."""
+        g_src, g_rows, g_flags = gather if gather is not None else ([], 0, None)
         self.C.gemm(A, a_mn, B, b_mn, int(M), int(N), int(K), list(A2), B2, int(K2), int(section_n), int(epi),
                     out, out2, bias, res, gate, int(split_row), cos, sin, int(rope_cols), int(head_dim), pre,
                     float(alpha), int(splits), int(block_n), self.status, self.limit_ns, list(g_src), int(g_rows),
-                    g_flags, int(g_epoch))
+                    g_flags)
 
     def _splits(self, tiles: int, k: int) -> int:
         kb = (k + 63) // 64

@@ -132,10 +132,10 @@ class PeerComm(TorchComm):
     # ---------------------------------------------------------------- all-gather fused into a GEMM
     def gather_spec(self, shard: torch.Tensor, rows_per_rank: int, flags: torch.Tensor):
         """Arguments for ``NativeKernels.linear_allgather``: every rank's shard
-        of a row-sharded weight (symmetric buffer of ``rows_per_rank`` rows),
-        this rank's per-N-tile flags (zeroed int32, reused across calls) and a
-        fresh epoch.  No barrier is needed: the shards are written once."""
-        return self.peer_ptrs(shard), int(rows_per_rank), flags, self.next_epoch()
+        of a row-sharded weight (symmetric buffer of ``rows_per_rank`` rows)
+        and this rank's int32 per-N-tile counters (reset by each call).  No
+        barrier is needed: the shards are written once."""
+        return self.peer_ptrs(shard), int(rows_per_rank), flags
 
     # ---------------------------------------------------------------- AdaLN GEMV + all-gather
     def adaln_project(self, temb: torch.Tensor, w_rows: torch.Tensor, b_rows: torch.Tensor,

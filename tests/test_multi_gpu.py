@@ -121,7 +121,7 @@ def _collectives(rank: int, port: int, errors, multimem: str = "0") -> None:
         w_local = torch.empty(n, k, dtype=torch.bfloat16, device=dev)
         flags = torch.zeros((n + 255) // 256, dtype=torch.int32, device=dev)
         ref = K.linear(x, w_full, bias)
-        for _ in range(2):   # the second call reuses the flags with a new epoch
+        for _ in range(2):   # the second call reuses (and resets) the tile counters
             w_local.zero_()
             y = K.linear_allgather(x, w_local, comm.gather_spec(w_shard, rows, flags), bias=bias)
             torch.cuda.synchronize()
