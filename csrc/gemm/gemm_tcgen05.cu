@@ -541,7 +541,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const long units = (r1 - r0) * units_per_row;
         const long per_cta = (units + gridDim.x - 1) / gridDim.x;
         const long u_lo = min(units, blockIdx.x * per_cta), u_hi = min(units, u_lo + per_cta);
-        constexpr int kU = 4;
+        constexpr int kU = 8;   // 8 KB of loads in flight per CTA (NVLink latency needs depth)
         for (long base = u_lo + gt; base < u_hi; base += kGatherThreads * kU) {
           uint4 v[kU];
 #pragma unroll
