@@ -26,7 +26,7 @@ import sys
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
-BASELINE_S_PER_CYCLE = 912.718721   # published reference number (16x A100-40GB, world16)
+REFERENCE_S_PER_CYCLE = 912.718721   # the reference's published cycle time (16x A100-40GB, world16)
 METRIC = "s per matched DMD cycle @768x1344x124f (max over ranks); peak GiB/rank"
 
 
@@ -160,7 +160,7 @@ def main() -> None:
             "ms_per_step": round(dev_ms / args.steps, 2),
             "higher_is_better": False,
             "scaling": "weak",
-            "vs_baseline": round(s_per_cycle / BASELINE_S_PER_CYCLE, 5) if headline else None,
+            "vs_baseline": round(s_per_cycle / REFERENCE_S_PER_CYCLE, 5) if headline else None,
             "dtype": "bf16",
             "data": "synthetic: seeded N(0,1) video/audio latents and text conditioning; random-init weights",
             "impl": args.impl,
