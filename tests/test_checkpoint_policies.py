@@ -213,3 +213,23 @@ def test_saved_tensor_offload_preserves_gradients():
     torch.testing.assert_close(v.grad, v_ref.grad)
     torch.testing.assert_close(cand.weight.grad, ref.weight.grad)
     assert scope.stats["pack_count"] > 0 and scope.stats["offload_count"] > 0
+
+
+def test_staging_target_choice(monkeypatch):
+    """`auto` keeps boundary slabs on the host while every local rank's slabs
+    fit in half the node's available RAM, else in HBM; explicit targets win;
+    CPU devices always stage on the host."""
+    from h3_a100.memory import boundary
+
+    gib = 1024**3
+    monkeypatch.setattr(boundary, "host_available_bytes", lambda: 200 * gib)
+    cuda = torch.device("cuda", 0)
+    assert boundary.choose_staging_target("auto", 20 * gib, 4, cuda) == "host"      # 80 <= 100
+    assert boundary.choose_staging_target("auto", 20 * gib, 8, cuda) == "device"    # 160 > 100
+    assert boundary.choose_staging_target("host", 20 * gib, 8, cuda) == "host"
+    assert boundary.choose_staging_target("device", 1, 1, cuda) == "device"
+    assert boundary.choose_staging_target("auto", 20 * gib, 8, torch.device("cpu")) == "host"
+    monkeypatch.setattr(boundary, "host_available_bytes", lambda: 0)                # unreadable meminfo
+    assert boundary.choose_staging_target("auto", 1, 1, cuda) == "device"
+    with pytest.raises(ValueError):
+        boundary.choose_staging_target("disk", 1, 1, cuda)
