@@ -560,6 +560,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (u < u_hi) reinterpret_cast<uint4*>(p.g_dst)[r0 * units_per_row + u] = v[k];
           }
         }
+        // The tile is read by TMA (async proxy) in other CTAs: order this
+        // thread's generic-proxy stores before the async proxy on the writer
+        // side too, then publish the slice with a release add.
+        fence_async_global();
         asm volatile("bar.sync 1, %0;" ::"n"(kGatherThreads) : "memory");
         if (gt == 0) {
           __threadfence();

@@ -30,7 +30,7 @@ except ImportError as exc:  # pragma: no cover - exercised only on broken instal
         "h3_a100._C (the sm_100a extension) is not built; run `python setup.py build_ext --inplace`"
     ) from exc
 
-from .torch_kernels import GatedResidual, Rope, TorchKernels
+from .torch_kernels import GatedResidual, Rope
 
 EPI_BF16, EPI_GELU, EPI_ROPE = _C.EPI_BF16, _C.EPI_GELU, _C.EPI_ROPE
 EPI_GATED_RES, EPI_GELU_BWD, EPI_F32_ACC = _C.EPI_GATED_RES, _C.EPI_GELU_BWD, _C.EPI_F32_ACC
@@ -56,8 +56,9 @@ class NativeKernels:
         self.limit_ns = int(wait_limit_s * 1e9)
         self.sms = _num_sms(device)
         self._ones = torch.ones(1, dtype=torch.float32, device=device)
-        self._ref = TorchKernels()   # attention backward until the tcgen05 version lands
-        self.attention_native = hasattr(_C, "attention_fwd")
+        missing = [name for name in ("gemm", "attention_fwd", "attention_bwd") if not hasattr(_C, name)]
+        if missing:
+            raise RuntimeError(f"the sm_100a extension lacks {missing}; rebuild it (python setup.py build_ext --inplace)")
 
     # ------------------------------------------------------------ bookkeeping
     def launch_count(self) -> int:
@@ -170,8 +171,9 @@ class NativeKernels:
             self._gemm(dy[:, s * width:(s + 1) * width], True, u[:, s * r:(s + 1) * r], True, width, r, t,
                        EPI_F32_ACC, grad_b[s * width:(s + 1) * width], splits=self._splits(tiles, t), block_n=128)
 
-    def gelu_bwd(self, dy, pre):  # only reached when not fused into linear_dx
-        return self._ref.gelu_bwd(dy, pre)
+    def gelu_bwd(self, dy, pre):
+        raise NotImplementedError("the native kernel set fuses the GELU backward into the FF2 input-gradient "
+                                  "GEMM: call linear_dx(..., gelu_pre=pre)")
 
     def rope_bwd(self, dqkv, rope: Rope):
         self.C.rope_inverse_(dqkv, rope.cos, rope.sin, rope.section_width * len(rope.sections), rope.head_dim)
@@ -179,15 +181,13 @@ class NativeKernels:
 
     # ------------------------------------------------------------ attention
     def attention_fwd(self, qkv, heads, head_dim):
-        if self.attention_native:
-            o, lse = self.C.attention_fwd(qkv, int(heads), int(head_dim), self.status, self.limit_ns)
-            return o, lse
-        return self._ref.attention_fwd(qkv, heads, head_dim)
+        o, lse = self.C.attention_fwd(qkv, int(heads), int(head_dim), self.status, self.limit_ns)
+        return o, lse
 
     def attention_bwd(self, qkv, o, lse, do, heads, head_dim):
-        if self.attention_native and hasattr(self.C, "attention_bwd") and lse is not None:
-            return self.C.attention_bwd(qkv, o, lse, do, int(heads), int(head_dim), self.status, self.limit_ns)
-        return self._ref.attention_bwd(qkv, o, lse, do, heads, head_dim)
+        if lse is None:
+            raise ValueError("the tcgen05 attention backward needs the forward's log-sum-exp rows")
+        return self.C.attention_bwd(qkv, o, lse, do, int(heads), int(head_dim), self.status, self.limit_ns)
 
     # ------------------------------------------------------------ small projections
     def adaln_project(self, temb, w, b):

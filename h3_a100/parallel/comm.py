@@ -37,6 +37,9 @@ class TorchComm:
         self._free: dict[int, list[tuple[torch.Tensor, object]]] = defaultdict(list)
         self.bytes_gathered = 0
         self.bytes_reduced = 0
+        # Optional ``StallLedger``: when set, every wait of the compute stream
+        # on a prefetched gather is timed as exposed all-gather time.
+        self.ledger = None
 
     # ---------------- buffers ----------------
     def alloc_shard(self, numel: int, dtype: torch.dtype) -> torch.Tensor:
@@ -88,8 +91,12 @@ class TorchComm:
 
     def wait(self, pending: _Pending) -> torch.Tensor:
         if pending.event is not None:
-            torch.cuda.current_stream(self.device).wait_event(pending.event)
-            pending.out.record_stream(torch.cuda.current_stream(self.device))
+            stream = torch.cuda.current_stream(self.device)
+            if self.ledger is not None:
+                self.ledger.wait("all_gather", pending.event, stream)
+            else:
+                stream.wait_event(pending.event)
+            pending.out.record_stream(stream)
         return pending.out
 
     # ---------------- small collectives ----------------

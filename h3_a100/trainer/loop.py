@@ -75,9 +75,27 @@ class LoopMixin:
             fake = self._fake_steps(samples)
         self.timer.stop("critic_phase")
         values = torch.stack([dmd.reshape(()).float(), fake.reshape(()).float()]).cpu()
+        self._record_cycle_times()
         if validate:
             self._validate_cycle(current_iter)
         return {"dmd": float(values[0]), "fake": float(values[1])}
+
+    def _record_cycle_times(self) -> None:
+        """Per-phase device seconds and exposed (non-overlapped) collective time of this cycle.
+
+        Phases come from CUDA events on the compute stream; ``optimizer_step``
+        is the device time of the six optimizer steps, which contain the LoRA
+        gradient reduce-scatter (fused with clip + AdamW on the peer-memory
+        transport); ``all_gather`` is the time the compute stream stalled on
+        the prefetched frozen-weight gathers.
+        """
+        phases = self.timer.take()
+        stalls = self.stall_ledger.collect()
+        self.last_cycle_receipt["phases_s"] = {k: round(v / 1e3, 4) for k, v in sorted(phases.items())}
+        self.last_cycle_receipt["exposed_comm_s"] = {
+            "all_gather": round(stalls.get("all_gather", 0.0) / 1e3, 4),
+            "optimizer_step_incl_reduce_scatter": round(phases.get("optimizer_step", 0.0) / 1e3, 4),
+        }
 
     # ---------------------------------------------------------------- steps
     def _next_sample(self, samples, stage: str):
@@ -104,7 +122,9 @@ class LoopMixin:
                     (result["loss"] / self.gradient_accumulation_iters).backward()
                 self.residency("after_student_backward")
             running = running + result["dmd"] / self.gradient_accumulation_iters
+        self.timer.start("optimizer_step")
         opt.step(self.lr_schedulers[STUDENT].get_last_lr()[0])
+        self.timer.stop("optimizer_step")
         self.lr_schedulers[STUDENT].step()
         opt.zero_grad()
         return running
@@ -112,11 +132,15 @@ class LoopMixin:
     def _fake_steps(self, samples) -> torch.Tensor:
         running = torch.zeros((), device=self.device)
         if self.reorder_critic_rollouts:
+            self.timer.start("critic_prepare")
             with nvtx("h3/critic_prepare_5xG"):
                 groups = [self._prepare_one_fake_group(samples, i) for i in range(self.fake_update_ratio)]
+            self.timer.stop("critic_prepare")
+            self.timer.start("critic_updates")
             for group in groups:
                 with nvtx("h3/critic_update_F"):
                     running = running + self._apply_one_fake_group(group) / self.fake_update_ratio
+            self.timer.stop("critic_updates")
             return running
         for i in range(self.fake_update_ratio):
             group = self._prepare_one_fake_group(samples, i)
@@ -145,7 +169,9 @@ class LoopMixin:
                     (loss / len(group)).backward()
             self.model.drop_adaln_key(item.cache_key)
             total = total + loss.detach() / len(group)
+        self.timer.start("optimizer_step")
         opt.step(self.lr_schedulers[FAKE].get_last_lr()[0])
+        self.timer.stop("optimizer_step")
         self.lr_schedulers[FAKE].step()
         opt.zero_grad()
         return total
@@ -184,7 +210,8 @@ class LoopMixin:
             raise RuntimeError(f"checkpoint-boundary CPU staging contract failed at outer iteration "
                                f"{current_iter}: {'; '.join(errors)}")
         offloaded = int(reg.stats["offloaded_storage_bytes"]) - int(self._boundary_start.get("offloaded_storage_bytes", 0))
-        self.last_cycle_receipt["boundary"] = {**observed, "offloaded_gib": offloaded / 1024**3}
+        self.last_cycle_receipt["boundary"] = {**observed, "offloaded_gib": offloaded / 1024**3,
+                                               "staging": self.boundary_staging_report()}
         logger.info("[h3-a100][boundary-offload] iter={} rank={} policy={} observed={} offloaded_gib={:.2f}",
                     current_iter, pdist.get_rank(), reg.receipt()["policy"], observed, offloaded / 1024**3)
 

@@ -28,7 +28,7 @@ from ..models.lora import FAKE, STUDENT
 from ..parallel import distributed as pdist
 from ..utils.log import logger
 from ..utils.memory import ResidencyLogger, log_cuda_memory
-from ..utils.timing import PhaseTimer
+from ..utils.timing import PhaseTimer, StallLedger
 from .checkpointing import CheckpointMixin
 from .loop import LoopMixin
 from .matched_contract import FIXED_END_STEP_IDX, MatchedCycleCensus
@@ -145,6 +145,7 @@ class H3DmdTrainer(CheckpointMixin, LoopMixin, DMDRuntimeMixin):
         self.boundary_pool: PinnedSlabPool | None = None
         self.host_rng = torch.Generator().manual_seed(self.seed + pdist.get_rank())
         self.timer = PhaseTimer(enabled=True)
+        self.stall_ledger = StallLedger()
         self.residency = ResidencyLogger(self)
         self.metrics: list[dict] = []
         self.last_cycle_receipt: dict[str, Any] = {}
@@ -211,6 +212,7 @@ class H3DmdTrainer(CheckpointMixin, LoopMixin, DMDRuntimeMixin):
     def setup(self, resume_ckpt_path: str | None = None, *, comm=None) -> None:
         model = self.model
         self.comm = comm or self._build_comm()
+        self.comm.ledger = self.stall_ledger
         pad = 4 * max(1, self.comm.world_size)
         model.prepare_shared_backbone(student_lora=self.student_lora_config, fake_lora=self.fake_lora_config,
                                       cache_enabled=self.adaln_cache_enabled,
@@ -284,6 +286,20 @@ class H3DmdTrainer(CheckpointMixin, LoopMixin, DMDRuntimeMixin):
                     "boundary_events={} legacy_threshold_offload={}", self.activation_policy,
                     self.activation_checkpoint_segment_size, self.boundary_offload_pin_memory,
                     self.boundary_staging_target, self.boundary_offload_events, self.activation_offload_enabled)
+
+    def boundary_staging_report(self) -> dict[str, Any]:
+        """Where the checkpoint boundaries went: the reference pins them in host memory.
+
+        ``device`` keeps the same copies and counters in HBM slabs; it is not
+        like-for-like with the reference's host staging (no PCIe traffic).
+        """
+        pool = self.boundary_pool
+        if pool is None:
+            return {"policy": self.activation_policy, "target": None, "pinned": False,
+                    "like_for_like_with_reference": False}
+        return {"policy": self.activation_policy, "target": pool.target, "pinned": bool(pool.pin_memory),
+                "slab_gib": round(pool.allocated_bytes / 1024**3, 2),
+                "like_for_like_with_reference": pool.target == "host" and bool(pool.pin_memory)}
 
     def _boundary_bytes_per_rank(self, model) -> int:
         """Bytes of one grad forward's boundaries (one bf16 hidden state per block)."""

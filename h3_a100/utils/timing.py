@@ -60,6 +60,53 @@ class PhaseTimer:
         self._events.clear()
         self.totals_ms.clear()
 
+    def take(self) -> dict[str, float]:
+        """Totals since the last ``take`` (resolves pending events), then reset."""
+        out = self.collect()
+        self.reset()
+        return out
+
 
 def max_over_ranks(values: dict[str, float]) -> dict[str, float]:
     return {k: pdist.all_reduce_max(v) for k, v in sorted(values.items())}
+
+
+class StallLedger:
+    """Device time a stream spends blocked on another stream's event, by kind.
+
+    ``wait(kind, event)`` makes the current stream wait on ``event`` and, on
+    CUDA, brackets the wait with two timing events on the waiting stream: the
+    first completes when the stream's earlier work is done, the second when
+    the awaited event has fired, so their distance is exactly the time the
+    stream sat idle waiting (zero when the awaited work finished first).  For
+    the communication stream's all-gathers this is the *exposed*
+    (non-overlapped) collective time the scaling report asks for.
+    """
+
+    def __init__(self) -> None:
+        self.cuda = torch.cuda.is_available()
+        self._pairs: dict[str, list] = defaultdict(list)
+        self.counts: dict[str, int] = defaultdict(int)
+
+    def wait(self, kind: str, event, stream=None) -> None:
+        if event is None:
+            return
+        stream = stream or torch.cuda.current_stream()
+        if not self.cuda:
+            stream.wait_event(event)
+            return
+        before = torch.cuda.Event(enable_timing=True)
+        after = torch.cuda.Event(enable_timing=True)
+        before.record(stream)
+        stream.wait_event(event)
+        after.record(stream)
+        self._pairs[kind].append((before, after))
+        self.counts[kind] += 1
+
+    def collect(self) -> dict[str, float]:
+        """Milliseconds stalled per kind since the last collect (synchronizes)."""
+        if self.cuda and self._pairs:
+            torch.cuda.synchronize()
+        out = {kind: float(sum(b.elapsed_time(a) for b, a in pairs)) for kind, pairs in self._pairs.items()}
+        self._pairs.clear()
+        return out

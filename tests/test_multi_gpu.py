@@ -1,7 +1,13 @@
 """Peer-memory collectives on 2 GPUs, compared with NCCL + the PyTorch oracle.
 
-Runs as spawned ranks (one per GPU, NCCL over 127.0.0.1, short process-group
-timeout).  Skipped when fewer than two GPUs are visible.
+Runs as spawned ranks (one per GPU, NCCL over 127.0.0.1, NVLS off, short
+process-group timeout).  Skipped when fewer than two GPUs are visible.
+
+No rank is ever killed: every device wait in the peer kernels is bounded and
+the process group times out after 120 s, so a failing rank ends on its own;
+the test joins the ranks and fails if one is still alive.  Only the unicast
+peer-load path runs here (no NVLink multicast objects are bound), so a rank
+that fails leaves no multicast-bound memory behind.
 """
 
 from __future__ import annotations
@@ -29,16 +35,16 @@ def _free_port() -> int:
 
 def _init(rank: int, port: int) -> torch.device:
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(WORLD),
-                      LOCAL_RANK=str(rank))
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     return dev
 
 
-def _collectives(rank: int, port: int, errors, multimem: str = "0") -> None:
+def _collectives(rank: int, port: int, errors) -> None:
     try:
-        os.environ["H3_P2P_MULTIMEM"] = multimem
+        os.environ["H3_P2P_MULTIMEM"] = "0"
         dev = _init(rank, port)
         from h3_a100.ops.native import NativeKernels
         from h3_a100.ops.torch_kernels import TorchKernels
@@ -171,12 +177,13 @@ def _spawn(fn, port, *extra):
         p.start()
     for p in procs:
         p.join(timeout=600)
-    for p in procs:
-        if p.is_alive():
-            p.kill()
     msgs = []
     while not errors.empty():
         msgs.append(errors.get())
+    alive = [r for r, p in enumerate(procs) if p.is_alive()]
+    if alive:
+        msgs.append(f"ranks {alive} still running after 600 s (bounded waits and the 120 s process-group "
+                    "timeout should have ended them)")
     return msgs, [p.exitcode for p in procs]
 
 
@@ -186,11 +193,9 @@ def two_gpus():
         pytest.skip("needs two GPUs")
 
 
-@pytest.mark.parametrize("multimem", ["0", "1"], ids=["unicast", "multimem"])
-def test_peer_collectives_match_nccl(two_gpus, multimem):
-    """Unicast peer loads/stores, and the NVLS multimem variant (falls back to
-    unicast where the fabric has no multicast objects)."""
-    msgs, codes = _spawn(_collectives, _free_port(), multimem)
+def test_peer_collectives_match_nccl(two_gpus):
+    """Unicast peer loads/stores against NCCL and the PyTorch oracle."""
+    msgs, codes = _spawn(_collectives, _free_port())
     assert not msgs, "\n".join(msgs)
     assert codes == [0] * WORLD
 
@@ -210,10 +215,13 @@ def test_dmd_cycle_p2p_matches_nccl(two_gpus):
         msgs = []
         while not errors.empty():
             msgs.append(errors.get())
+        alive = [r for r, p in enumerate(procs) if p.is_alive()]
+        assert not alive, f"ranks {alive} of the {kind} cycle still running after 900 s"
         assert not msgs, "\n".join(msgs)
         out[kind] = results.get(timeout=5)
     (_, l_nccl, s_nccl), (_, l_p2p, s_p2p) = out["nccl"], out["p2p"]
     for a, b in zip(l_nccl, l_p2p):
-        assert abs(a["fake"] - b["fake"]) <= 2e-2 * max(1.0, abs(a["fake"])), (l_nccl, l_p2p)
-        assert abs(a["dmd"] - b["dmd"]) <= 5e-2 * max(1e-3, abs(a["dmd"])) + 1e-6, (l_nccl, l_p2p)
+        # same arithmetic, different summation order of the fp32 gradient reduction
+        assert abs(a["fake"] - b["fake"]) <= 5e-3 * max(1.0, abs(a["fake"])), (l_nccl, l_p2p)
+        assert abs(a["dmd"] - b["dmd"]) <= 2e-2 * max(1e-3, abs(a["dmd"])) + 1e-6, (l_nccl, l_p2p)
     assert abs(s_nccl - s_p2p) <= 1e-2 * max(1.0, abs(s_nccl)), (s_nccl, s_p2p)

@@ -53,6 +53,32 @@ def test_noalloc_matches_regular_entry_point_twice(entry, shape_a, shape_b):
         torch.testing.assert_close(grad, ref_grad, rtol=1e-4, atol=1e-6)
 
 
+@pytest.mark.parametrize("samples,per_sample", [(3, 5000), (MAX_SAMPLES, 300)])
+def test_noalloc_multi_sample_matches_fp32_formula(entry, samples, per_sample):
+    """Several samples per call: per-sample normalisers (one grid row each), the
+    second accumulator half and the final sum over samples, against the fp32
+    PyTorch statement of the DMD loss, on two calls in a row (the second call
+    finds the first call's sums in the shared scratch and must clear them)."""
+    from h3_a100.trainer.dmd_math import dmd_direction, dmd_loss
+
+    _, fn = entry
+    torch.manual_seed(1)
+    for call in range(2):
+        gen = torch.randn(samples, per_sample, device="cuda") * (1.0 + call)
+        real = torch.randn(samples, per_sample, device="cuda")
+        # per-sample scale so every sample has its own normaliser
+        real = real * torch.linspace(0.5, 2.0, samples, device="cuda")[:, None]
+        fake = real + 0.1 * torch.randn(samples, per_sample, device="cuda")
+        loss = torch.full((1,), -1.0, device="cuda")
+        grad = torch.full_like(gen, float("nan"))
+        assert _call(fn, gen, fake, real, loss, grad, samples) == 0
+        torch.cuda.synchronize()
+        ref_grad = dmd_direction(gen, fake, real)
+        ref_loss = dmd_loss(gen, fake, real)
+        torch.testing.assert_close(grad, ref_grad, rtol=1e-4, atol=1e-5)
+        torch.testing.assert_close(loss[0], ref_loss, rtol=1e-4, atol=1e-6)
+
+
 def test_noalloc_rejects_too_many_samples(entry):
     _, fn = entry
     gen = torch.zeros(MAX_SAMPLES + 1, 8, device="cuda")
