@@ -1,15 +1,21 @@
 """Checkpoint-boundary staging to pinned host memory.
 
-Policy and counters follow the reference's ``checkpoint_boundary_cpu``
-(``h3_a100/checkpoint_boundary_offload.py:27-336``): every grad-enabled
-checkpoint call stages exactly one tensor, its first argument (the block's
-input hidden states), to host memory and brings it back when the block is
-replayed in backward.  A forward pre/post hook pair on the transformer counts
-grad forwards per role and requires ``expected_block_count`` checkpoint calls
-per grad forward; stats keys and fail-closed errors are the reference's.
+Policy kept from the reference's ``checkpoint_boundary_cpu``
+(``h3_a100/checkpoint_boundary_offload.py:27-336``): every grad-enabled block
+checkpoint stages exactly one tensor, the block's input hidden states, to
+host memory and brings it back when backward replays the block; grad
+forwards are counted per role and each must make one checkpoint per block.
+The counter names are the reference's, because the per-cycle receipt
+(6 grad forwards: 1 Student / 5 Fake, 300 checkpoint calls, 300 copies) is
+expressed in them.
 
-What differs is the data path.  The reference copies synchronously
-(``copy_(non_blocking=False)``, ``:117,133``).  Here:
+What differs is who stages and how.  The reference finds the boundary
+through saved-tensor hooks inside a wrapped checkpoint function and counts
+forwards in module hooks; here the checkpoint (``BlockCheckpointing``)
+hands ``BoundaryStaging`` the block input directly (``save`` / ``restore``)
+and brackets each DiT forward with ``begin_forward`` / ``end_forward``, so one
+copy per checkpoint holds by construction.  And the reference copies
+synchronously (``copy_(non_blocking=False)``, ``:117,133``).  Here:
 
 * the device->host copy runs on a dedicated copy stream after an event on
   the compute stream, into a slab from a pinned pool that is allocated once
@@ -26,10 +32,9 @@ import json
 import threading
 import time
 from collections import defaultdict
-from contextlib import contextmanager
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 from pathlib import Path
-from typing import Any, Callable, Iterator
+from typing import Any
 
 import torch
 
@@ -42,12 +47,8 @@ STAT_KEYS = (
     "checkpoint_call_count",
     "grad_checkpoint_call_count",
     "cpu_copy_count",
-    "pack_count",
-    "unpack_count",
-    "duplicate_pack_count",
-    "policy_filter_keep_count",
-    "non_strided_keep_count",
-    "zero_stride_keep_count",
+    "restore_count",
+    "abandoned_count",
     "offloaded_logical_bytes",
     "offloaded_storage_bytes",
     "student_grad_forward_count",
@@ -55,19 +56,11 @@ STAT_KEYS = (
     "other_grad_forward_count",
     "prefetch_count",
 )
+_ROLE_COUNTERS = {"student": "student_grad_forward_count", "fake": "fake_grad_forward_count"}
 
 
 def _nbytes(t: torch.Tensor) -> int:
     return int(t.numel() * t.element_size())
-
-
-def _signature(t: torch.Tensor):
-    return tuple(int(s) for s in t.shape), str(t.dtype), _nbytes(t)
-
-
-def _alias(t: torch.Tensor):
-    return (int(t.untyped_storage().data_ptr()), int(t.storage_offset()),
-            tuple(t.shape), tuple(t.stride()), str(t.dtype))
 
 
 def _pinned_empty(numel: int, dtype: torch.dtype) -> torch.Tensor:
@@ -169,11 +162,6 @@ class PinnedSlabPool:
 
 
 @dataclass(eq=False)
-class _Keep:
-    tensor: torch.Tensor
-
-
-@dataclass(eq=False)
 class _Staged:
     slab: torch.Tensor
     shape: tuple
@@ -183,7 +171,6 @@ class _Staged:
     d2h_done: Any = None           # torch.cuda.Event on the copy stream
     upload: torch.Tensor | None = None
     h2d_done: Any = None
-    remaining_unpacks: int = 1
 
 
 class BoundaryStager:
@@ -255,11 +242,9 @@ class BoundaryStager:
             if index > 0:
                 # Backward replays blocks in reverse: the previous boundary is next.
                 self._start_upload(self._stack[index - 1])
-        staged.remaining_unpacks -= 1
-        if staged.remaining_unpacks < 0:
-            raise RuntimeError("checkpoint-boundary tensor unpacked too many times")
-        if staged.remaining_unpacks == 0:
-            self._recycle(staged)
+        if index is None:
+            raise RuntimeError("checkpoint boundary restored twice (or never staged by this stager)")
+        self._recycle(staged)
         return out
 
     def _recycle(self, staged: _Staged) -> None:
@@ -270,200 +255,96 @@ class BoundaryStager:
     def live(self) -> int:
         return len(self._stack)
 
+    def abandon(self) -> int:
+        """Recycle boundaries whose backward never ran (an aborted step); returns how many."""
+        left = list(self._stack)
+        self._stack.clear()
+        for staged in left:
+            self.pool.release(staged.slab, after_event=staged.d2h_done)
+        return len(left)
 
-class _BoundaryScope:
-    """saved-tensor hooks for one checkpoint call, matching only the boundary signature."""
 
-    def __init__(self, *, target: torch.Tensor, stager: BoundaryStager, require_cuda: bool,
-                 stats: dict[str, int]) -> None:
-        if target.layout != torch.strided:
-            raise RuntimeError("checkpoint boundary input must be strided")
-        if any(s > 1 and st == 0 for s, st in zip(target.shape, target.stride())):
-            raise RuntimeError("checkpoint boundary input cannot be a zero-stride view")
-        if require_cuda and not target.is_cuda:
-            raise RuntimeError(f"checkpoint boundary input must be CUDA, got {target.device}")
-        self.signature = _signature(target)
-        self.stager = stager
-        self.stats = stats
-        self._by_alias: dict[Any, _Staged] = {}
-        self.copies = 0
+class BoundaryStaging:
+    """The ``checkpoint_boundary_cpu`` policy: counters, fail-closed checks and the stager.
 
-    def _pack(self, tensor: torch.Tensor):
-        self.stats["pack_count"] += 1
-        if _signature(tensor) != self.signature:
-            self.stats["policy_filter_keep_count"] += 1
-            return _Keep(tensor)
-        if tensor.layout != torch.strided:
-            self.stats["non_strided_keep_count"] += 1
-            return _Keep(tensor)
-        if any(s > 1 and st == 0 for s, st in zip(tensor.shape, tensor.stride())):
-            self.stats["zero_stride_keep_count"] += 1
-            return _Keep(tensor)
-        alias = _alias(tensor)
-        existing = self._by_alias.get(alias)
-        if existing is not None:
-            existing.remaining_unpacks += 1
-            self.stats["duplicate_pack_count"] += 1
-            return existing
-        staged = self.stager.stage_out(tensor)
-        self._by_alias[alias] = staged
-        self.copies += 1
+    Driven by ``BlockCheckpointing``: ``begin_forward`` / ``end_forward``
+    bracket every DiT forward, ``note_call`` sees every checkpoint call,
+    ``save`` stages the input of each grad checkpoint and ``restore`` brings it
+    back in backward.  With ``event_path`` a JSON line per saved boundary and
+    per completed grad forward is appended (an existing file is never
+    overwritten).
+    """
+
+    policy = POLICY_NAME
+
+    def __init__(self, *, expected_block_count: int = PRODUCTION_BLOCK_COUNT, pool: PinnedSlabPool | None = None,
+                 pin_memory: bool = True, require_cuda: bool = True, event_path: Path | None = None) -> None:
+        self.expected_block_count = int(expected_block_count)
+        self.pin_memory = bool(pin_memory)
+        self.require_cuda = bool(require_cuda)
+        self.stats = dict.fromkeys(STAT_KEYS, 0)
+        self.stager = BoundaryStager(pool or PinnedSlabPool(pin_memory), self.stats)
+        self.event_path = None if event_path is None else Path(event_path)
+        if self.event_path is not None:
+            if self.event_path.exists():
+                raise FileExistsError(f"refusing to overwrite checkpoint-boundary events: {self.event_path}")
+            self.event_path.parent.mkdir(parents=True, exist_ok=True)
+        self._lock = threading.Lock()
+        self._role = "unknown"
+        self._block = 0
+
+    # ------------------------------------------------------------ forward bracket
+    def begin_forward(self, role: str, grad: bool) -> None:
+        self.stats["transformer_forward_count"] += 1
+        self._role, self._block = str(role), 0
+        if grad and self.stager.live():
+            # The previous grad forward's backward never ran: free its slabs.
+            self.stats["abandoned_count"] += self.stager.abandon()
+
+    def end_forward(self, role: str, grad: bool, calls: int) -> None:
+        if not grad:
+            return
+        if calls != self.expected_block_count:
+            raise RuntimeError(f"checkpoint-boundary staging: grad forward made {calls} checkpoint calls, "
+                               f"expected {self.expected_block_count}")
+        self.stats["grad_transformer_forward_count"] += 1
+        self.stats[_ROLE_COUNTERS.get(str(role), "other_grad_forward_count")] += 1
+        self._event({"event": "grad_forward_complete", "role": str(role), "checkpoint_calls": calls,
+                     "copies_total": self.stats["cpu_copy_count"]})
+
+    def note_call(self, grad: bool) -> None:
+        self.stats["checkpoint_call_count"] += 1
+        if grad:
+            self.stats["grad_checkpoint_call_count"] += 1
+
+    # ------------------------------------------------------------ boundaries
+    def save(self, hidden: torch.Tensor) -> _Staged:
+        if self.require_cuda and not hidden.is_cuda:
+            raise RuntimeError(f"checkpoint boundary must be a CUDA tensor, got {hidden.device}")
+        if self._block >= self.expected_block_count:
+            raise RuntimeError(f"more than {self.expected_block_count} boundaries in one grad forward")
+        staged = self.stager.stage_out(hidden)
         self.stats["cpu_copy_count"] += 1
-        self.stats["offloaded_logical_bytes"] += _nbytes(tensor)
-        self.stats["offloaded_storage_bytes"] += staged.slab.numel() * staged.slab.element_size()
+        self.stats["offloaded_logical_bytes"] += _nbytes(hidden)
+        self.stats["offloaded_storage_bytes"] += _nbytes(staged.slab)
+        self._event({"event": "boundary_saved", "block": self._block, "role": self._role,
+                     "shape": list(hidden.shape), "dtype": str(hidden.dtype), "bytes": _nbytes(hidden)})
+        self._block += 1
         return staged
 
-    def _unpack(self, packed):
-        self.stats["unpack_count"] += 1
-        if isinstance(packed, _Keep):
-            return packed.tensor
-        if not isinstance(packed, _Staged):
-            raise TypeError(f"unexpected checkpoint-boundary saved object: {type(packed)!r}")
-        return self.stager.stage_in(packed)
+    def restore(self, staged: _Staged) -> torch.Tensor:
+        self.stats["restore_count"] += 1
+        return self.stager.stage_in(staged)
 
-    @contextmanager
-    def context(self) -> Iterator[None]:
-        with torch.autograd.graph.saved_tensors_hooks(self._pack, self._unpack):
-            yield
-        if self.copies != 1:
-            raise RuntimeError(
-                f"checkpoint-boundary staging expected exactly one boundary copy, observed {self.copies}"
-            )
-        self._by_alias.clear()
-
-
-@dataclass
-class CheckpointBoundaryOffloadRegistration:
-    transformer: torch.nn.Module
-    original_checkpoint: Callable[..., Any]
-    pre_hook: Any
-    post_hook: Any
-    role_getter: Callable[[], str]
-    event_path: Path | None
-    expected_block_count: int
-    pin_memory: bool
-    stats: dict[str, int]
-    stager: BoundaryStager | None = None
-    closed: bool = False
-    extra: dict = field(default_factory=dict)
+    # ------------------------------------------------------------ reporting
+    def _event(self, payload: dict[str, Any]) -> None:
+        if self.event_path is None:
+            return
+        with self._lock, self.event_path.open("a", encoding="utf-8") as fh:
+            fh.write(json.dumps({"t": round(time.time(), 6), **payload}, sort_keys=True) + "\n")
 
     def receipt(self) -> dict[str, Any]:
-        return {
-            "policy": POLICY_NAME,
-            "expected_block_count": self.expected_block_count,
-            "pin_memory": self.pin_memory,
-            "event_path": None if self.event_path is None else str(self.event_path),
-            "stats": dict(self.stats),
-            "closed": self.closed,
-        }
-
-    def remove(self) -> None:
-        if self.closed:
-            return
-        self.pre_hook.remove()
-        self.post_hook.remove()
-        self.transformer._gradient_checkpointing_func = self.original_checkpoint
-        self.closed = True
-
-
-def install_checkpoint_boundary_cpu_offload(
-    transformer: torch.nn.Module,
-    *,
-    role_getter: Callable[[], str],
-    event_path: Path | None = None,
-    pin_memory: bool = True,
-    expected_block_count: int = PRODUCTION_BLOCK_COUNT,
-    require_cuda: bool = True,
-    pool: PinnedSlabPool | None = None,
-) -> CheckpointBoundaryOffloadRegistration:
-    """Wrap ``transformer._gradient_checkpointing_func`` with boundary staging."""
-    blocks = getattr(transformer, "transformer_blocks", None)
-    if blocks is None or len(blocks) != int(expected_block_count):
-        raise RuntimeError(
-            "checkpoint-boundary CPU staging requires native per-block layout: "
-            f"expected {expected_block_count} transformer blocks, got {0 if blocks is None else len(blocks)}"
-        )
-    if not bool(getattr(transformer, "gradient_checkpointing", False)):
-        raise RuntimeError("checkpoint-boundary CPU staging requires gradient checkpointing")
-    original = getattr(transformer, "_gradient_checkpointing_func", None)
-    if not callable(original):
-        raise RuntimeError("transformer has no callable gradient checkpoint function")
-    path = None if event_path is None else Path(event_path)
-    if path is not None:
-        path.parent.mkdir(parents=True, exist_ok=True)
-        if path.exists():
-            raise FileExistsError(f"refusing to overwrite checkpoint-boundary events: {path}")
-
-    stats = dict.fromkeys(STAT_KEYS, 0)
-    stager = BoundaryStager(pool or PinnedSlabPool(pin_memory), stats)
-    state: dict[str, Any] = {"calls": 0, "grad": False, "role": "unknown"}
-    lock = threading.Lock()
-
-    def write_event(payload: dict[str, Any]) -> None:
-        if path is None:
-            return
-        with lock, path.open("a", encoding="utf-8") as fh:
-            fh.write(json.dumps({"time_unix": time.time(), **payload}, sort_keys=True) + "\n")
-
-    def wrapped(function: Callable[..., Any], *args: Any, **kwargs: Any) -> Any:
-        index = int(state["calls"])
-        state["calls"] = index + 1
-        stats["checkpoint_call_count"] += 1
-        if not torch.is_grad_enabled():
-            return original(function, *args, **kwargs)
-        if index >= int(expected_block_count):
-            raise RuntimeError(f"checkpoint call count exceeded expected {expected_block_count}: index={index}")
-        if not args or not torch.is_tensor(args[0]):
-            raise RuntimeError(f"checkpoint block {index} has no tensor boundary input")
-        stats["grad_checkpoint_call_count"] += 1
-        boundary = args[0]
-        scope = _BoundaryScope(target=boundary, stager=stager, require_cuda=require_cuda, stats=stats)
-        before = int(stats["cpu_copy_count"])
-        with scope.context():
-            result = original(function, *args, **kwargs)
-        write_event({
-            "event": "checkpoint_boundary_saved",
-            "block_index": index,
-            "role": state["role"],
-            "shape": list(boundary.shape),
-            "dtype": str(boundary.dtype),
-            "logical_bytes": _nbytes(boundary),
-            "new_cpu_copies": int(stats["cpu_copy_count"]) - before,
-        })
-        return result
-
-    def pre_hook(_module, _inputs) -> None:
-        state["calls"] = 0
-        state["grad"] = bool(torch.is_grad_enabled())
-        state["role"] = str(role_getter())
-        stats["transformer_forward_count"] += 1
-
-    def post_hook(_module, _inputs, _output) -> None:
-        if not state["grad"]:
-            return
-        calls = int(state["calls"])
-        if calls != int(expected_block_count):
-            raise RuntimeError(f"native checkpoint call count mismatch: {calls} != {expected_block_count}")
-        stats["grad_transformer_forward_count"] += 1
-        role = str(state["role"])
-        key = {"student": "student_grad_forward_count", "fake": "fake_grad_forward_count"}.get(
-            role, "other_grad_forward_count")
-        stats[key] += 1
-        write_event({"event": "grad_transformer_forward_complete", "role": role,
-                     "checkpoint_calls": calls, "cpu_copies_total": int(stats["cpu_copy_count"])})
-
-    pre = transformer.register_forward_pre_hook(pre_hook)
-    post = transformer.register_forward_hook(post_hook, always_call=True)
-    transformer._gradient_checkpointing_func = wrapped
-    return CheckpointBoundaryOffloadRegistration(
-        transformer=transformer,
-        original_checkpoint=original,
-        pre_hook=pre,
-        post_hook=post,
-        role_getter=role_getter,
-        event_path=path,
-        expected_block_count=int(expected_block_count),
-        pin_memory=bool(pin_memory),
-        stats=stats,
-        stager=stager,
-    )
+        return {"policy": self.policy, "expected_block_count": self.expected_block_count,
+                "pin_memory": self.pin_memory, "target": self.stager.pool.target,
+                "event_path": None if self.event_path is None else str(self.event_path),
+                "stats": dict(self.stats)}

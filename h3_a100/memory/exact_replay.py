@@ -1,105 +1,97 @@
-"""Exact AdaLN replay audit around the checkpoint function.
+"""Exact AdaLN replay audit, run by the checkpoint itself.
 
-Same contract as the reference (``h3_a100/exact_adaln_replay.py:50-223``):
-the outermost checkpoint wrapper captures the active AdaLN key when a block's
-checkpoint is created (it must exist and be complete for every block), enters
-that key around the original execution *and* the backward replay, and
-requires each execution to take exactly one cache hit and no miss.  Per cycle
-the trainer checks 300 wraps / 600 scoped executions / 600 hits / 0 misses
-(1 Student + 5 Fake grad forwards x 50 blocks).
+Contract kept from the reference (``h3_a100/exact_adaln_replay.py:50-223``):
+a grad-enabled block checkpoint may only be created under a complete AdaLN
+key, and each execution of the block, the original one and the backward
+replay, must read its modulation from that key's cached table exactly once
+and never miss (never fall back to the projection).  Per cycle that is
+300 checkpoints / 600 executions / 600 hits / 0 misses for 1 Student + 5 Fake
+grad forwards of 50 blocks; the stat names are the reference's, since the
+cycle receipt is expressed in them.
 
-Chain installed by the trainer:
-``exact AdaLN scope -> boundary staging -> native checkpoint``.
+Mechanism here: the block call carries its key (``call.key``) and the number
+of modulation reads one execution makes (``call.fetches``: 1 for a block, the
+block count for a checkpoint segment).  ``BlockCheckpointing`` calls
+``note_checkpoint`` when it creates a checkpoint and routes every execution
+through ``execute``, which hands the call a counting fetch and checks the
+counts when the execution returns.  Nothing ambient is captured or restored.
 """
 
 from __future__ import annotations
 
-from dataclasses import dataclass
-from typing import Any, Callable
+from typing import Any
 
-from ..models.adaln import AdaLNCacheController
+import torch
 
-EXPECTED_CYCLE_COUNTS = {
-    "checkpoint_wrap_count": 300,
-    "scoped_execution_count": 600,
-    "cache_hit_count": 600,
-    "cache_miss_count": 0,
-    "captured_key_missing_count": 0,
-    "captured_key_incomplete_count": 0,
-    "unexpected_hit_delta_count": 0,
-}
-
-
-def expected_cycle_counts(blocks: int, grad_forwards: int = 6) -> dict[str, int]:
-    wraps = blocks * grad_forwards
-    return {**EXPECTED_CYCLE_COUNTS, "checkpoint_wrap_count": wraps,
-            "scoped_execution_count": 2 * wraps, "cache_hit_count": 2 * wraps}
+STAT_KEYS = (
+    "checkpoint_wrap_count",
+    "scoped_execution_count",
+    "cache_hit_count",
+    "cache_miss_count",
+    "captured_key_missing_count",
+    "captured_key_incomplete_count",
+    "unexpected_hit_delta_count",
+)
 
 
-@dataclass
-class ExactAdaLNReplayRegistration:
-    transformer: Any
-    controller: AdaLNCacheController
-    original_checkpoint: Callable[..., Any]
-    stats: dict[str, int]
-    closed: bool = False
-
-    def receipt(self) -> dict[str, Any]:
-        return {"policy": "exact_adaln_checkpoint_replay_scope", "stats": dict(self.stats), "closed": self.closed}
-
-    def remove(self) -> None:
-        if not self.closed:
-            self.transformer._gradient_checkpointing_func = self.original_checkpoint
-            self.closed = True
-
-
-def install_exact_adaln_checkpoint_replay_scope(
-    transformer: Any, controller: AdaLNCacheController, *, expected_block_count: int = 50
-) -> ExactAdaLNReplayRegistration:
-    original = getattr(transformer, "_gradient_checkpointing_func", None)
-    if not callable(original):
-        raise RuntimeError("transformer has no callable checkpoint function")
-    if not bool(getattr(transformer, "gradient_checkpointing", False)):
-        raise RuntimeError("exact AdaLN replay scope requires gradient checkpointing")
-    stats = {key: 0 for key in EXPECTED_CYCLE_COUNTS}
-
-    def wrapped(function: Callable[..., Any], *args: Any, **kwargs: Any) -> Any:
-        active = controller.current_scope()
-        key = active.key
-        if key is None:
-            stats["captured_key_missing_count"] += 1
-            raise RuntimeError(
-                "Exact AdaLN checkpoint replay has no active cache key; "
-                "refusing to fall back to the AdaLN projection bank."
-            )
-        if not controller.has_complete_key(key, expected_block_count):
-            stats["captured_key_incomplete_count"] += 1
-            raise RuntimeError(f"Exact AdaLN cache key {key!r} is incomplete before checkpoint creation")
-        persistent = bool(active.persistent)
-        stats["checkpoint_wrap_count"] += 1
-
-        def scoped(*fn_args: Any, **fn_kwargs: Any) -> Any:
-            before = controller.stats()
-            stats["scoped_execution_count"] += 1
-            try:
-                with controller.scope(key, persistent=persistent):
-                    return function(*fn_args, **fn_kwargs)
-            finally:
-                after = controller.stats()
-                hits, misses = after.hits - before.hits, after.misses - before.misses
-                stats["cache_hit_count"] += hits
-                stats["cache_miss_count"] += misses
-                if misses != 0:
-                    raise RuntimeError(f"Exact AdaLN replay cache miss for key={key!r}; miss_delta={misses}")
-                if hits != 1:
-                    stats["unexpected_hit_delta_count"] += 1
-                    raise RuntimeError(f"Exact AdaLN replay expected one cache hit per block, got {hits} for key={key!r}")
-
-        return original(scoped, *args, **kwargs)
-
-    transformer._gradient_checkpointing_func = wrapped
-    return ExactAdaLNReplayRegistration(transformer, controller, original, stats)
+def expected_cycle_counts(blocks: int, grad_forwards: int = 6, segment_size: int = 1) -> dict[str, int]:
+    """Audit counters of one matched cycle (``grad_forwards`` grad DiT forwards)."""
+    wraps = grad_forwards * -(-int(blocks) // int(segment_size))
+    expected = dict.fromkeys(STAT_KEYS, 0)
+    expected.update(checkpoint_wrap_count=wraps, scoped_execution_count=2 * wraps,
+                    cache_hit_count=2 * grad_forwards * int(blocks))
+    return expected
 
 
 def cycle_delta(stats: dict[str, int], start: dict[str, int]) -> dict[str, int]:
-    return {key: int(stats[key]) - int(start.get(key, 0)) for key in EXPECTED_CYCLE_COUNTS}
+    return {key: int(stats[key]) - int(start.get(key, 0)) for key in STAT_KEYS}
+
+
+class ReplayAudit:
+    policy = "exact_adaln_checkpoint_replay_scope"
+
+    def __init__(self, cache) -> None:
+        self.cache = cache
+        self.stats = dict.fromkeys(STAT_KEYS, 0)
+
+    def note_checkpoint(self, call: Any) -> None:
+        """A grad checkpoint is being created for ``call``: its key must be cached for every block."""
+        key = getattr(call, "key", None)
+        if key is None:
+            self.stats["captured_key_missing_count"] += 1
+            raise RuntimeError("exact AdaLN replay: a block checkpoint was created without an AdaLN key; "
+                               "the projection bank is never used as a fallback")
+        if not self.cache.complete(key):
+            self.stats["captured_key_incomplete_count"] += 1
+            raise RuntimeError(f"exact AdaLN replay: key {key!r} has no complete modulation table "
+                               "when the checkpoint is created")
+        self.stats["checkpoint_wrap_count"] += 1
+
+    def execute(self, call: Any, hidden: torch.Tensor) -> torch.Tensor:
+        """Run one execution of ``call`` with counted modulation reads, then check the counts."""
+        counts = [0, 0]   # hits, misses
+        cache = self.cache
+
+        def fetch(key, block):
+            value = cache.fetch(key, block)
+            counts[value is None] += 1
+            return value
+
+        self.stats["scoped_execution_count"] += 1
+        try:
+            out = call(hidden, fetch=fetch)
+        finally:
+            self.stats["cache_hit_count"] += counts[0]
+            self.stats["cache_miss_count"] += counts[1]
+        hits, misses = counts
+        expected = int(getattr(call, "fetches", 1))
+        if misses:
+            raise RuntimeError(f"exact AdaLN replay miss for key {getattr(call, 'key', None)!r} ({misses} misses)")
+        if hits != expected:
+            self.stats["unexpected_hit_delta_count"] += 1
+            raise RuntimeError(f"exact AdaLN replay expected {expected} modulation read(s) per execution, "
+                               f"got {hits} for key {getattr(call, 'key', None)!r}")
+        return out
+
+    def receipt(self) -> dict[str, Any]:
+        return {"policy": self.policy, "stats": dict(self.stats)}

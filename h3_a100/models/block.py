@@ -134,13 +134,12 @@ class _BlockFn(torch.autograd.Function):
 
 
 class H3Block(nn.Module):
-    """Frozen block weights (possibly sharded) + the AdaLN projection slot."""
+    """Frozen block weights (possibly sharded); the AdaLN projection lives in the DiT's bank."""
 
     WEIGHT_NAMES = ("qkv_weight", "qkv_bias", "out_weight", "out_bias",
                     "ff0_weight", "ff0_bias", "ff2_weight", "ff2_bias")
 
-    def __init__(self, hidden: int, ffn: int, prefix: str, *, adaln: nn.Module | None,
-                 dtype: torch.dtype, device) -> None:
+    def __init__(self, hidden: int, ffn: int, prefix: str, *, dtype: torch.dtype, device) -> None:
         super().__init__()
         self.prefix = prefix
         self.hidden, self.ffn = hidden, ffn
@@ -152,8 +151,6 @@ class H3Block(nn.Module):
         self.out_weight, self.out_bias = frozen(hidden, hidden), frozen(hidden)
         self.ff0_weight, self.ff0_bias = frozen(ffn, hidden), frozen(ffn)
         self.ff2_weight, self.ff2_bias = frozen(hidden, ffn), frozen(hidden)
-        if adaln is not None:
-            self.adaln_proj = adaln
         object.__setattr__(self, "_unit", None)   # sharded-parameter unit, if any
         object.__setattr__(self, "_on_backward_done", None)
 

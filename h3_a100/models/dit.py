@@ -22,6 +22,7 @@ every rank); there is no checkpoint to load.
 
 from __future__ import annotations
 
+import contextlib
 import math
 from dataclasses import dataclass, field
 
@@ -29,7 +30,9 @@ import torch
 import torch.nn.functional as F
 from torch import nn
 
+from ..memory.checkpoint import BlockCheckpointing
 from ..ops.torch_kernels import Rope
+from .adaln import AdaLNBank
 from .block import BlockContext, H3Block
 from .rope import rope_tables
 
@@ -172,20 +175,24 @@ class H3DiT(nn.Module):
         self.time_embedder = TimeEmbedder(cfg.freq_dim, cfg.time_embed_dim, dtype, device)
         self.token_refiner = nn.Module()
         self.token_refiner.refiner_blocks = nn.ModuleList(
-            [H3Block(h, cfg.ffn, f"token_refiner.refiner_blocks.{i}", adaln=None, dtype=dtype, device=device)
+            [H3Block(h, cfg.ffn, f"token_refiner.refiner_blocks.{i}", dtype=dtype, device=device)
              for i in range(cfg.num_refiner_blocks)]
         )
         self.transformer_blocks = nn.ModuleList(
-            [H3Block(h, cfg.ffn, f"transformer_blocks.{i}",
-                     adaln=AdaLNProjection(cfg.time_embed_dim, h, dtype, device), dtype=dtype, device=device)
+            [H3Block(h, cfg.ffn, f"transformer_blocks.{i}", dtype=dtype, device=device)
              for i in range(cfg.num_blocks)]
         )
+        # One projection per joint block, owned by the bank (each its own sharded unit).
+        self.adaln_bank = AdaLNBank([AdaLNProjection(cfg.time_embed_dim, h, dtype, device)
+                                     for _ in range(cfg.num_blocks)])
         self.norm_out = nn.Linear(cfg.time_embed_dim, 2 * h, dtype=dtype, device=device)
         self.proj_out = nn.Linear(h, pc, dtype=dtype, device=device)
         self.proj_out_audio = nn.Linear(h, cfg.audio_channels, dtype=dtype, device=device) if cfg.audio_channels else None
         self.requires_grad_(False)
-        self.gradient_checkpointing = False
-        self._gradient_checkpointing_func = None
+        self.checkpointing: BlockCheckpointing | None = None
+        # Optional ``probe(block_index, "before"|"after")`` around every joint
+        # block execution (per-block memory attribution); None costs nothing.
+        self.block_probe = None
         self._rope_cache: dict = {}
         self.kernels = None
 
@@ -211,11 +218,14 @@ class H3DiT(nn.Module):
             if isinstance(module, AdaLNProjection):
                 object.__setattr__(module, "kernels", kernels)
 
-    def enable_gradient_checkpointing(self, fn=None) -> None:
-        from ..memory.checkpoint import native_checkpoint
+    def enable_gradient_checkpointing(self, segment_size: int = 1) -> BlockCheckpointing:
+        """Checkpoint every block (or every ``segment_size`` blocks) in grad forwards."""
+        self.checkpointing = BlockCheckpointing(self.cfg.num_blocks, segment_size=segment_size)
+        return self.checkpointing
 
-        self.gradient_checkpointing = True
-        self._gradient_checkpointing_func = fn or native_checkpoint
+    @property
+    def gradient_checkpointing(self) -> bool:
+        return self.checkpointing is not None
 
     # ---------------- layout helpers ----------------
     def token_layout(self, video_shape, audio_shape, text_len: int) -> TokenLayout:
@@ -253,20 +263,38 @@ class H3DiT(nn.Module):
         return self.time_embedder(freq.to(self.time_embedder.linear_1.weight.dtype))
 
     def adaln_projections(self):
-        bank = getattr(self, "adaln_bank", None)
-        if bank is not None:
-            return list(bank.projections)
-        return [blk.adaln_proj for blk in self.transformer_blocks]
+        return list(self.adaln_bank.projections)
+
+    def project_adaln(self, index: int, temb: torch.Tensor) -> torch.Tensor:
+        """Block ``index``'s modulation ``[R, 6, H]`` fp32 from the time embedding.
+
+        Uses the row-sharded projection when the bank is sharded across ranks
+        (``sharded_projections``), else the bank's own weights.
+        """
+        sharded = getattr(self, "sharded_projections", None)
+        if sharded:
+            return sharded[index](temb).view(temb.shape[0], 6, self.cfg.hidden)
+        return self.adaln_bank[index](temb)
 
     # ---------------- forward ----------------
     def forward(self, video: torch.Tensor, audio: torch.Tensor | None, text: torch.Tensor,
-                timesteps: torch.Tensor, *, lora_store=None, adaln_key=None, controller=None):
+                timesteps: torch.Tensor, *, role: str = "student", lora_store=None, adaln_key=None,
+                modulations=None):
         """Predict (video velocity, audio velocity).
 
         ``timesteps``: [2] (video t, audio t) in [0, num_train_timesteps].
+        ``role``: the logical role of this forward (counted by the checkpoint plan).
         ``lora_store``: the active role's LoRAStore, or None for the Teacher.
-        ``adaln_key``: cache key whose modulations were precomputed.
+        ``adaln_key`` + ``modulations``: the ``ModulationCache`` key whose table
+        was precomputed; without them each block projects ``temb`` itself.
         """
+        plan = self.checkpointing
+        grad = torch.is_grad_enabled()
+        with plan.forward(role, grad) if plan is not None else contextlib.nullcontext():
+            return self._forward(video, audio, text, timesteps, lora_store, adaln_key, modulations,
+                                 plan if grad else None)
+
+    def _forward(self, video, audio, text, timesteps, lora_store, adaln_key, modulations, plan):
         kern = self.kernels
         dtype = self.patch_embed.weight.dtype
         layout = self.token_layout(video.shape, None if audio is None else audio.shape, text.shape[1])
@@ -303,18 +331,15 @@ class H3DiT(nn.Module):
 
         with torch.no_grad():
             temb = self.time_embedding(timesteps)
-        if controller is None:
-            controller = getattr(self, "_h3_adaln_controller", None)
-        use_ckpt = self.gradient_checkpointing and torch.is_grad_enabled() and self._gradient_checkpointing_func is not None
-        for index, blk in enumerate(self.transformer_blocks):
-            if use_ckpt:
-                # The block call fetches its modulation itself, once per execution
-                # (original forward and replay), so replay is audited per block.
-                ctx = block_ctx(blk, None, layout.split, rope)
-                x = self._gradient_checkpointing_func(_BlockCall(blk, ctx, index, controller, adaln_key, temb), x)
-            else:
-                ctx = block_ctx(blk, self._modulation(index, blk, temb, controller, adaln_key), layout.split, rope)
-                x = blk(x, ctx)
+        calls = [BlockCall(blk, block_ctx(blk, None, layout.split, rope), index, adaln_key, modulations,
+                           self.project_adaln, temb, self.block_probe)
+                 for index, blk in enumerate(self.transformer_blocks)]
+        if plan is not None:
+            for unit in plan.segments(calls):
+                x = plan.run(unit, x)
+        else:
+            for call in calls:
+                x = call(x)
 
         # --- output head ---
         with torch.no_grad():
@@ -329,40 +354,39 @@ class H3DiT(nn.Module):
             v_audio = a_tok.t().unsqueeze(0)
         return v_video, v_audio
 
-    def _modulation(self, index, blk, temb, controller, key):
-        if controller is not None and key is not None:
-            hit = controller.lookup(key, index)
-            if hit is not None:
-                return hit[0]
-            raise RuntimeError(f"AdaLN modulation for key {key!r} block {index} was not precomputed")
-        return blk.adaln_proj(temb)[0] if controller is not None else blk.adaln_proj(temb)
 
+class BlockCall:
+    """One joint block with everything its execution needs, for the original run and replay.
 
-class _BlockCall:
-    """Callable handed to the checkpoint function: one block with captured context.
-
-    The modulation tensor, RoPE table and LoRA views are captured when the
-    forward runs, so checkpoint replay recomputes the block with exactly the
-    same inputs.  Each execution re-reads the modulation through the cache
-    (one counted hit), which is what the exact-replay audit checks.
+    The LoRA views, RoPE table and AdaLN key are captured when the forward
+    builds the call, so a checkpoint replay recomputes the block on exactly
+    the same inputs.  Each execution reads the block's modulation once,
+    through ``fetch(key, index)`` when it is given one (the replay audit's
+    counting fetch) or the cache's own ``fetch``; with no key it projects
+    ``temb`` itself (AdaLN cache disabled).
     """
 
-    def __init__(self, block, ctx, index, controller, key, temb):
-        self.block, self.ctx, self.index = block, ctx, index
-        self.controller, self.key, self.temb = controller, key, temb
+    __slots__ = ("block", "ctx", "index", "key", "cache", "project", "temb", "probe")
+    fetches = 1
 
-    def __call__(self, x):
-        controller = self.controller
-        key = self.key
-        if controller is not None and key is None:
-            key = controller.current_scope().key
-        if controller is not None and key is not None:
-            hit = controller.lookup(key, self.index)
-            if hit is None:
-                raise RuntimeError(f"exact AdaLN replay miss for key {key!r} block {self.index}")
-            modulation = hit[0]
-        else:
-            modulation = self.block.adaln_proj(self.temb)
-            modulation = modulation[0] if isinstance(modulation, tuple) else modulation
-        ctx = BlockContext(**{**self.ctx.__dict__, "modulation": modulation})
-        return self.block(x, ctx)
+    def __init__(self, block, ctx, index, key, cache, project, temb, probe=None):
+        self.block, self.ctx, self.index = block, ctx, index
+        self.key, self.cache, self.project, self.temb = key, cache, project, temb
+        self.probe = probe
+
+    def modulation(self, fetch=None) -> torch.Tensor:
+        if self.key is not None and self.cache is not None:
+            value = (fetch or self.cache.fetch)(self.key, self.index)
+            if value is None:
+                raise RuntimeError(f"AdaLN modulation for key {self.key!r} block {self.index} was not precomputed")
+            return value
+        return self.project(self.index, self.temb)
+
+    def __call__(self, x, fetch=None):
+        ctx = BlockContext(**{**self.ctx.__dict__, "modulation": self.modulation(fetch)})
+        if self.probe is None:
+            return self.block(x, ctx)
+        self.probe(self.index, "before")
+        out = self.block(x, ctx)
+        self.probe(self.index, "after")
+        return out

@@ -7,7 +7,10 @@ disjoint optimizers; the AdaLN bank is installed before sharding; modulations
 are precomputed per exact timestep key.  Differences by design:
 
 * the role is an explicit argument of every forward (``predict_velocity``);
-  ``role_scope`` is kept as the public context manager and for logging;
+  ``role_scope`` only sets the default role of calls that name none;
+* AdaLN keys are explicit too: ``precompute_adaln`` builds a key's table and
+  every forward/backward that reads it names it (``adaln_scope`` holds the
+  table resident meanwhile);
 * adapters are flat per-role buffers (``LoRAStore``), not PEFT modules;
 * sharding is this package's own runtime (``h3_a100.parallel.sharded``), with
   the reference's unit plan: time embedder, each AdaLN projection, each
@@ -17,7 +20,6 @@ are precomputed per exact timestep key.  Differences by design:
 from __future__ import annotations
 
 import contextlib
-import contextvars
 import os
 from collections.abc import Iterator
 from typing import Any
@@ -28,7 +30,7 @@ from safetensors.torch import load_file, save_file
 from ..config import get
 from ..parallel.sharded import ShardedProjection, ShardedUnit, link_order
 from ..utils.log import logger
-from .adaln import AdaLNCacheController, adaln_bank, adaln_controller, install_adaln_cache
+from .adaln import ModulationCache
 from .block import H3Block
 from .dit import DiTConfig, H3DiT
 from .lora import FAKE, STUDENT, TEACHER, TRAINABLE_ROLES, LoRALayout, LoRAStore, target_modules_supported
@@ -71,7 +73,8 @@ class H3SharedBackbone:
         self.transformer = H3DiT(self.dit_config, dtype=self.param_dtype, device=device)
         self.transformer.init_weights(self.base_seed)
         self.transformer.set_kernels(kernels)
-        self._role: contextvars.ContextVar[str] = contextvars.ContextVar("h3_role", default=STUDENT)
+        self._default_role = STUDENT
+        self.modulations: ModulationCache | None = None
         self.lora: dict[str, LoRAStore] = {}
         self.units: list[ShardedUnit] = []
         self.projections: list[ShardedProjection] = []
@@ -87,7 +90,8 @@ class H3SharedBackbone:
             return
         dit = self.transformer
         dit.requires_grad_(False)
-        install_adaln_cache(dit, enabled=cache_enabled, max_dynamic_keys=max_dynamic_cache_keys)
+        self.modulations = ModulationCache.attach(dit.adaln_bank, dit.time_embedder, enabled=cache_enabled,
+                                                  max_dynamic_keys=max_dynamic_cache_keys)
         prefixes = [b.prefix for b in dit.token_refiner.refiner_blocks] + [b.prefix for b in dit.transformer_blocks]
         for role, lcfg in ((STUDENT, student_lora), (FAKE, fake_lora)):
             target_modules_supported(lcfg.get("target_modules", ()))
@@ -116,9 +120,9 @@ class H3SharedBackbone:
             units.append(unit)
         link_order(units)
         self.units = units
-        bank = adaln_bank(dit)
-        if comm.world_size > 1 and bank is not None:
-            self.projections = [ShardedProjection(p, comm, self.kernels) for p in bank.projections]
+        if comm.world_size > 1:
+            self.projections = [ShardedProjection(p, comm, self.kernels) for p in dit.adaln_bank.projections]
+            dit.sharded_projections = self.projections
         # time embedder, embeds and heads are small: kept replicated (root unit, not resharded).
         del root_reshard
         torch.cuda.empty_cache() if torch.cuda.is_available() else None
@@ -141,52 +145,41 @@ class H3SharedBackbone:
 
     @contextlib.contextmanager
     def role_scope(self, role: str) -> Iterator[None]:
+        """Default role of ``predict_velocity`` calls that name none, for the duration."""
         if role not in (STUDENT, FAKE, TEACHER):
             raise ValueError(f"unknown role {role!r}")
-        token = self._role.set(role)
+        previous, self._default_role = self._default_role, role
         try:
             yield
         finally:
-            self._role.reset(token)
+            self._default_role = previous
 
     def current_role(self) -> str:
-        return self._role.get()
+        return self._default_role
 
     # ------------------------------------------------------------------ AdaLN
-    def adaln_cache(self) -> AdaLNCacheController:
-        controller = adaln_controller(self.transformer)
-        if controller is None:
-            raise RuntimeError("AdaLN cache was not installed")
-        return controller
+    def adaln_cache(self) -> ModulationCache:
+        if self.modulations is None:
+            raise RuntimeError("the AdaLN modulation cache is set up by prepare_shared_backbone")
+        return self.modulations
 
     @contextlib.contextmanager
-    def adaln_scope(self, key: Any, *, persistent: bool = False) -> Iterator[None]:
-        with self.adaln_cache().scope(key, persistent=persistent):
+    def adaln_scope(self, key: Any) -> Iterator[None]:
+        """Keep ``key``'s modulation table resident while a forward or backward reads it."""
+        with self.adaln_cache().hold(key):
             yield
 
-    @torch.no_grad()
     def precompute_adaln(self, key: Any, timesteps: torch.Tensor, *, persistent: bool) -> None:
-        """Materialise every block's modulation for one exact timestep table."""
+        """Materialise every block's modulation for one exact timestep table (no-op if present)."""
         dit = self.transformer
-        bank = adaln_bank(dit)
-        controller = self.adaln_cache()
-        if bank is None:
-            raise RuntimeError("AdaLN projection bank is missing")
-        if controller.has_complete_key(key, len(bank.projections)):
-            return
-        temb = dit.time_embedding(timesteps.to(self.device))
-        hidden = self.dit_config.hidden
-        with controller.scope(key, persistent=persistent):
-            for index, projection in enumerate(bank.projections):
-                if self.projections:
-                    sharded = self.projections[index]
-                    fn = lambda t, s=sharded: s(t).view(t.shape[0], 6, hidden)  # noqa: E731
-                else:
-                    fn = projection
-                controller.get_or_compute(index, temb, fn)
+        if not self.adaln_cache().enabled:
+            return     # cache off: every block projects its own modulation
+        self.adaln_cache().build(key, persistent=persistent,
+                                 temb=lambda: dit.time_embedding(timesteps.to(self.device)),
+                                 project=dit.project_adaln)
 
     def drop_adaln_key(self, key: Any) -> None:
-        self.adaln_cache().drop(key)
+        self.adaln_cache().release(key)
 
     def log_adaln_stats(self, prefix: str = "[h3-a100]") -> None:
         s = self.adaln_cache().stats()
@@ -195,12 +188,14 @@ class H3SharedBackbone:
                     s.persistent_keys, s.dynamic_keys, s.bytes / 1024**2)
 
     # ------------------------------------------------------------------ forward
-    def predict_velocity(self, role: str, latents, timesteps: torch.Tensor, condition: dict, *, adaln_key=None):
+    def predict_velocity(self, role: str | None, latents, timesteps: torch.Tensor, condition: dict, *,
+                         adaln_key=None):
+        role = role or self._default_role
         video, audio = latents
-        with self.role_scope(role):
-            return self.transformer(video, audio, condition["text"], timesteps,
-                                    lora_store=self.lora_store(role), adaln_key=adaln_key,
-                                    controller=self.adaln_cache())
+        cache = self.modulations if (self.modulations is not None and self.modulations.enabled) else None
+        return self.transformer(video, audio, condition["text"], timesteps, role=role,
+                                lora_store=self.lora_store(role), adaln_key=adaln_key if cache else None,
+                                modulations=cache)
 
     # ------------------------------------------------------------------ LoRA IO
     def save_all_role_loras(self, student_dir: str, fake_dir: str, *, main_process: bool = True) -> None:

@@ -117,7 +117,7 @@ class LoopMixin:
                 self.residency("after_student_grad_forward")
                 if offload is not None:
                     offload.begin_backward()
-                with self.model.role_scope(STUDENT), self.model.adaln_scope(result["backward_key"], persistent=True):
+                with self.model.adaln_scope(result["backward_key"]):
                     self.matched_cycle_census.note_backward(STUDENT_ROLE)
                     (result["loss"] / self.gradient_accumulation_iters).backward()
                 self.residency("after_student_backward")
@@ -164,7 +164,7 @@ class LoopMixin:
                 loss = self.fake_loss(item)
                 if offload is not None:
                     offload.begin_backward()
-                with self.model.role_scope(FAKE), self.model.adaln_scope(item.cache_key, persistent=False):
+                with self.model.adaln_scope(item.cache_key):
                     self.matched_cycle_census.note_backward(FAKE_ROLE)
                     (loss / len(group)).backward()
             self.model.drop_adaln_key(item.cache_key)
@@ -178,10 +178,10 @@ class LoopMixin:
 
     # ---------------------------------------------------------------- checks
     def _begin_cycle_counters(self) -> None:
-        reg = self.boundary_offload_registration
-        self._boundary_start = None if reg is None else dict(reg.stats)
-        rep = self.exact_adaln_replay_registration
-        self._replay_start = None if rep is None else dict(rep.stats)
+        staging = self.boundary_staging
+        self._boundary_start = None if staging is None else dict(staging.stats)
+        audit = self.replay_audit
+        self._replay_start = None if audit is None else dict(audit.stats)
 
     def _validate_cycle(self, current_iter: int) -> None:
         if self.matched_compute_enabled:
@@ -190,7 +190,7 @@ class LoopMixin:
         self._validate_exact_replay_cycle(current_iter)
 
     def _validate_boundary_offload_cycle(self, current_iter: int) -> None:
-        reg = self.boundary_offload_registration
+        reg = self.boundary_staging
         if reg is None:
             return
         if self._boundary_start is None:
@@ -216,12 +216,13 @@ class LoopMixin:
                     current_iter, pdist.get_rank(), reg.receipt()["policy"], observed, offloaded / 1024**3)
 
     def _validate_exact_replay_cycle(self, current_iter: int) -> None:
-        rep = self.exact_adaln_replay_registration
+        rep = self.replay_audit
         if rep is None:
             return
         if self._replay_start is None:
             raise RuntimeError("exact AdaLN replay cycle baseline is missing")
-        expected = expected_cycle_counts(self.model.dit_config.num_blocks)
+        expected = expected_cycle_counts(self.model.dit_config.num_blocks,
+                                         segment_size=self.activation_checkpoint_segment_size)
         observed = cycle_delta(rep.stats, self._replay_start)
         errors = [f"{k}={observed[k]} expected={v}" for k, v in expected.items() if observed[k] != v]
         if errors:

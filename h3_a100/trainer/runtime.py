@@ -96,7 +96,7 @@ class DMDRuntimeMixin:
             key = ("rollout", int(step))
             self.model.precompute_adaln(key, self._timesteps(sig), persistent=True)
             with_grad = grad_enabled and step == end_step_idx
-            with torch.set_grad_enabled(with_grad), self.model.adaln_scope(key, persistent=True):
+            with torch.set_grad_enabled(with_grad), self.model.adaln_scope(key):
                 velocity = self._predict(STUDENT, xt, sig, condition, key)
             if with_grad:
                 backward_key = key
@@ -123,7 +123,7 @@ class DMDRuntimeMixin:
                          for g, n, s in zip(generated, noises, sigmas))
         score_key = self._next_score_key()
         self.model.precompute_adaln(score_key, self._timesteps(sigmas), persistent=False)
-        with torch.no_grad(), self.model.adaln_scope(score_key, persistent=False):
+        with torch.no_grad(), self.model.adaln_scope(score_key):
             v_fake = self._predict(FAKE, renoised, sigmas, condition, score_key)
             v_teacher = self._predict(TEACHER, renoised, sigmas, condition, score_key)
             x0_fake = tuple(None if v is None else K.x0_from_velocity(r, v, s)
@@ -151,7 +151,7 @@ class DMDRuntimeMixin:
     def fake_loss(self, item: PreparedFakeUpdate) -> torch.Tensor:
         K = self.kernels
         self.model.precompute_adaln(item.cache_key, self._timesteps(item.sigmas), persistent=False)
-        with self.model.adaln_scope(item.cache_key, persistent=False):
+        with self.model.adaln_scope(item.cache_key):
             v_fake = self._predict(FAKE, item.renoised, item.sigmas, item.condition, item.cache_key)
             loss = self.video_loss_weight * K.mse_loss(v_fake[0], item.generated[0].float() - item.noises[0])
             if v_fake[1] is not None and self.audio_loss_weight:

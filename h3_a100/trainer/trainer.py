@@ -21,13 +21,13 @@ import torch
 
 from ..config import env_flag, get, training_system_section
 from ..memory.boundary import POLICY_NAME as CHECKPOINT_BOUNDARY_CPU
-from ..memory.boundary import PinnedSlabPool, choose_staging_target, install_checkpoint_boundary_cpu_offload
-from ..memory.exact_replay import install_exact_adaln_checkpoint_replay_scope
-from ..memory.saved_tensor_offload import maybe_saved_tensor_offload
+from ..memory.boundary import BoundaryStaging, PinnedSlabPool, choose_staging_target
+from ..memory.exact_replay import ReplayAudit
+from ..memory.saved_tensor_offload import offload_scope
 from ..models.lora import FAKE, STUDENT
 from ..parallel import distributed as pdist
 from ..utils.log import logger
-from ..utils.memory import ResidencyLogger, log_cuda_memory
+from ..utils.memory import BlockResidencyProbe, ResidencyLogger, log_cuda_memory
 from ..utils.timing import PhaseTimer, StallLedger
 from .checkpointing import CheckpointMixin
 from .loop import LoopMixin
@@ -140,8 +140,8 @@ class H3DmdTrainer(CheckpointMixin, LoopMixin, DMDRuntimeMixin):
         self.data = None
         self.optimizers: dict[str, FlatAdamW] = {}
         self.lr_schedulers: dict[str, LRSchedule] = {}
-        self.boundary_offload_registration = None
-        self.exact_adaln_replay_registration = None
+        self.boundary_staging: BoundaryStaging | None = None
+        self.replay_audit: ReplayAudit | None = None
         self.boundary_pool: PinnedSlabPool | None = None
         self.host_rng = torch.Generator().manual_seed(self.seed + pdist.get_rank())
         self.timer = PhaseTimer(enabled=True)
@@ -187,10 +187,10 @@ class H3DmdTrainer(CheckpointMixin, LoopMixin, DMDRuntimeMixin):
         return {"video": tuple(sample["video_latent"].shape), "audio": None if audio is None else tuple(audio.shape)}
 
     def _activation_offload_scope(self, component: str):
-        return maybe_saved_tensor_offload(
-            self.model.denoiser_module(), enabled=self.activation_offload_enabled, logical_component=component,
-            min_offload_bytes=self.activation_offload_min_bytes, pin_memory=self.activation_offload_pin_memory,
-            offload_cpu_tensors=self.device.type == "cpu")
+        return offload_scope(
+            self.model.denoiser_module(), enabled=self.activation_offload_enabled, label=component,
+            min_bytes=self.activation_offload_min_bytes, pin_memory=self.activation_offload_pin_memory,
+            include_cpu=self.device.type == "cpu")
 
     # ---------------------------------------------------------------- setup
     def _build_comm(self):
@@ -228,11 +228,13 @@ class H3DmdTrainer(CheckpointMixin, LoopMixin, DMDRuntimeMixin):
         shard_comm = self.comm if fsdp_enabled else _LocalComm(self.device)
         model.apply_sharding(shard_comm, block_reshard=bool(reshard.get("block_reshard", True)),
                              root_reshard=bool(reshard.get("root_reshard", False)))
+        plan = None
         if self.gradient_checkpointing:
-            dit.enable_gradient_checkpointing()
+            plan = dit.enable_gradient_checkpointing(self.activation_checkpoint_segment_size)
             if self.activation_checkpoint_segment_size > 1:
-                from ..memory.segments import group_calls  # noqa: F401  (diagnostic path)
-                raise NotImplementedError("segment_size > 1 is diagnostic-only and not wired into the DiT loop")
+                logger.info("[h3-a100] SAC activation checkpoint segments enabled segment_size={} blocks={} "
+                            "segments={} (diagnostic)", self.activation_checkpoint_segment_size,
+                            model.dit_config.num_blocks, plan.calls_per_grad_forward)
         if self.activation_policy == CHECKPOINT_BOUNDARY_CPU:
             event_path = None
             if self.boundary_offload_events:
@@ -243,11 +245,11 @@ class H3DmdTrainer(CheckpointMixin, LoopMixin, DMDRuntimeMixin):
                 self.boundary_staging_target, per_rank, local_ranks, self.device)
             self.boundary_pool = PinnedSlabPool(self.boundary_offload_pin_memory, self.boundary_staging_target,
                                                 self.device)
-            self.boundary_offload_registration = install_checkpoint_boundary_cpu_offload(
-                dit, role_getter=model.current_role, event_path=event_path,
-                pin_memory=self.boundary_offload_pin_memory,
-                expected_block_count=model.dit_config.num_blocks,
-                require_cuda=self.device.type == "cuda", pool=self.boundary_pool)
+            self.boundary_staging = BoundaryStaging(
+                expected_block_count=model.dit_config.num_blocks, pool=self.boundary_pool,
+                pin_memory=self.boundary_offload_pin_memory, require_cuda=self.device.type == "cuda",
+                event_path=event_path)
+            plan.attach_staging(self.boundary_staging)
         self.trainable_params = model.role_parameters(STUDENT)
         self.fake_trainable_params = model.role_parameters(FAKE)
         self._validate_shared_parameter_contract()
@@ -275,8 +277,12 @@ class H3DmdTrainer(CheckpointMixin, LoopMixin, DMDRuntimeMixin):
         if self.require_exact_replay and self.gradient_checkpointing:
             if not self.adaln_cache_enabled:
                 raise RuntimeError("exact replay requires exact AdaLN caching enabled")
-            self.exact_adaln_replay_registration = install_exact_adaln_checkpoint_replay_scope(
-                dit, model.adaln_cache(), expected_block_count=model.dit_config.num_blocks)
+            self.replay_audit = ReplayAudit(model.adaln_cache())
+            plan.attach_replay(self.replay_audit)
+        probe = BlockResidencyProbe()
+        if probe.enabled:
+            dit.block_probe = probe
+            self.block_residency = probe
         log_cuda_memory("after_setup")
         logger.info("[h3-a100] setup physical_backbones=1 logical_roles=3 student_params={} fake_params={} "
                     "sharded={} critic_reorder={} matched_compute={} kernels={}",

@@ -19,9 +19,8 @@ def _sample(i):
 
 def _complete(rank=0, world=8):
     c = MatchedCycleCensus(expected_world_size=world)
-    for _ in range(24):
-        c.note_forward("student", grad_enabled=False)
-    c.grad_forward_counts["student"] = 1
+    for i in range(24):
+        c.note_forward("student", grad_enabled=i == 23)
     for i in range(6):
         c.note_forward("fake", grad_enabled=i != 0)
     c.note_forward("teacher", grad_enabled=False)
@@ -42,15 +41,31 @@ def test_exact_inventory_passes():
 
 
 def test_missing_forward_fails():
-    c = _complete()
-    c.forward_counts["student"] -= 1
+    c = MatchedCycleCensus()
+    for _ in range(23):
+        c.note_forward("student", grad_enabled=False)
     assert any("forward_counts" in e for e in c.validate_local())
 
 
-def test_reused_sample_fails_locally():
+def test_extra_backward_fails():
     c = _complete()
-    c.samples[3]["identity"] = c.samples[0]["identity"]
+    c.note_backward("fake")
+    assert any("backward_counts" in e for e in c.validate_local())
+
+
+def test_reused_sample_fails_locally():
+    c = MatchedCycleCensus()
+    for stage in EXPECTED_SAMPLE_STAGES:
+        c.note_sample(stage, _sample(7))
     assert any("reused" in e for e in c.validate_local())
+
+
+def test_stage_order_is_checked():
+    c = _complete()
+    snap = c.snapshot()
+    snap["samples"][0], snap["samples"][1] = snap["samples"][1], snap["samples"][0]
+    errors = validate_global_snapshots([snap], expected_world_size=1, require_unique_samples=True)
+    assert any("sample stages" in e for e in errors)
 
 
 @pytest.mark.parametrize("world", [8, 16])
@@ -70,7 +85,8 @@ def test_wrong_world_size_fails():
 def test_identity_requires_meta():
     with pytest.raises(RuntimeError):
         sample_identity({"meta": {}})
-    assert sample_identity({"meta": {"row_index": 3, "id": "a"}}) == '{"id":"a","row_index":"3"}'
+    assert sample_identity({"meta": {"row_index": 3, "id": "a"}}) == "id=a|row_index=3"
+    assert sample_identity({"meta": {"row_index": 3, "id": "a"}}) != sample_identity({"meta": {"row_index": 4, "id": "a"}})
 
 
 def test_unknown_role_rejected():
