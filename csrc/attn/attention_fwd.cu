@@ -6,8 +6,11 @@
 // already applied by the QKV GEMM epilogue); o is [T, H] bf16, lse fp32.
 // Head dim D = 128.
 //
-// One CTA per (pair of 128-query tiles, head), 320 threads:
-//   warp 0      TMA: Q_0, Q_1 once, then K_j / V_j into a 2-stage ring
+// One CTA per (pair of 128-query tiles, head), 384 threads:
+//   warp 0      TMA: Q_0, Q_1 once, then K_0 V_0 K_1 V_1 ... through a ring of
+//               five 32 KB slots; a K slot is released as soon as both S MMAs
+//               that read it are done, a V slot once both PV MMAs are, so the
+//               next tiles' loads start ~1.5 KV steps before they are needed
 //   warp 1      tcgen05.mma issuer (one thread), per KV tile j:
 //                 S_t = Q_t K_j^T         into TMEM S_t (t = 0, 1)
 //                 O_t += P_t V_j          P_t read from TMEM (the .ts form),
@@ -55,7 +58,9 @@ constexpr int kRegsHigh = 216;
 static_assert(128 * kRegsLow + kQTiles * 128 * kRegsHigh == kThreads * kLaunchRegs, "register split");
 constexpr int kChunk = 128 * 64 * 2;    // 128 rows x 64 bf16 (one 128B-swizzled column chunk)
 constexpr int kTileBytes = 2 * kChunk;  // 128 rows x 128 bf16
-constexpr int kSmem = 1024 + kTileBytes * (kQTiles + 4) + 512;  // Q x2, K[2], V[2]
+constexpr int kSlots = 5;               // K/V ring: K_j in slot 2j % 5, V_j in slot (2j+1) % 5
+constexpr int kSmem = 1024 + kTileBytes * (kQTiles + kSlots) + 512;  // Q x2, ring
+static_assert(kSmem <= 232448, "attention forward shared memory");
 constexpr float kRescaleThreshold = 8.0f;                      // log2 units
 
 struct FwdParams {
@@ -219,10 +224,14 @@ __device__ __forceinline__ float row_exp_pack(uint32_t tS, const uint32_t (&r)[k
   return sa + sb;
 }
 
+__device__ __forceinline__ int ring_slot(int n) { return n % kSlots; }
+__device__ __forceinline__ uint32_t ring_phase(int n) { return static_cast<uint32_t>((n / kSlots) & 1); }
+
 // Producer warpgroup roles: warp 0 issues the TMA loads, warp 1 the MMAs.
+// Load sequence n = 0, 1, 2, ...: K_{n/2} for even n, V_{n/2} for odd n.
 __device__ __forceinline__ void producer_warps(const CUtensorMap& tm, const FwdParams& p, int warp, uint8_t* sQ,
-                                               uint8_t* sK, uint8_t* sV, uint64_t* q_full, uint64_t* kv_full,
-                                               uint64_t* kv_empty, uint64_t* s_full, uint64_t* p_full,
+                                               uint8_t* ring, uint64_t* q_full, uint64_t* slot_full,
+                                               uint64_t* slot_empty, uint64_t* s_full, uint64_t* p_full,
                                                uint64_t* o_done, uint64_t* drain, volatile int* abort_flag,
                                                uint32_t tmem, int head, int q0, int n_kv, uint64_t limit) {
   constexpr uint32_t kIdescS = umma_idesc_bf16(kBQ, kBKV, false, false);
@@ -236,35 +245,38 @@ __device__ __forceinline__ void producer_warps(const CUtensorMap& tm, const FwdP
         tma_load_2d(sQ + t * kTileBytes, &tm, q_full, xq, q0 + t * kBQ);
         tma_load_2d(sQ + t * kTileBytes + kChunk, &tm, q_full, xq + 64, q0 + t * kBQ);
       }
-      int issued_phase[2] = {-1, -1};
-      for (int j = 0; j < n_kv && !*abort_flag; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&kv_empty[st], ph ^ 1u, limit, abort_flag)) {
-          report_status(p.status, kStatusTimeoutEmpty, j);
+      int issued_phase[kSlots];
+#pragma unroll
+      for (int s = 0; s < kSlots; ++s) issued_phase[s] = -1;
+      for (int n = 0; n < 2 * n_kv && !*abort_flag; ++n) {
+        const int slot = ring_slot(n);
+        const uint32_t ph = ring_phase(n);
+        if (!mbar_wait(&slot_empty[slot], ph ^ 1u, limit, abort_flag)) {
+          report_status(p.status, kStatusTimeoutEmpty, n);
           *abort_flag = 1;
           break;
         }
-        const int y = j * kBKV;
-        mbar_arrive_expect_tx(&kv_full[st], 2 * kTileBytes);
-        tma_load_2d(sK + st * kTileBytes, &tm, &kv_full[st], xk, y);
-        tma_load_2d(sK + st * kTileBytes + kChunk, &tm, &kv_full[st], xk + 64, y);
-        tma_load_2d(sV + st * kTileBytes, &tm, &kv_full[st], xv, y);
-        tma_load_2d(sV + st * kTileBytes + kChunk, &tm, &kv_full[st], xv + 64, y);
-        issued_phase[st] = static_cast<int>(ph);
+        const int x = (n & 1) ? xv : xk, y = (n >> 1) * kBKV;
+        mbar_arrive_expect_tx(&slot_full[slot], kTileBytes);
+        tma_load_2d(ring + slot * kTileBytes, &tm, &slot_full[slot], x, y);
+        tma_load_2d(ring + slot * kTileBytes + kChunk, &tm, &slot_full[slot], x + 64, y);
+        issued_phase[slot] = static_cast<int>(ph);
       }
+      // Never leave a TMA write in flight into this CTA's shared memory.
       volatile int never = 0;
       mbar_wait(q_full, 0, limit, &never);
-      for (int st = 0; st < 2; ++st)
-        if (issued_phase[st] >= 0) mbar_wait(&kv_full[st], issued_phase[st], limit, &never);
+      for (int s = 0; s < kSlots; ++s)
+        if (issued_phase[s] >= 0) mbar_wait(&slot_full[s], issued_phase[s], limit, &never);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (elect_one()) {
       bool any = false;
       bool ok = mbar_wait(q_full, 0, limit, abort_flag);
+      auto wait_slot = [&](int n) { return mbar_wait(&slot_full[ring_slot(n)], ring_phase(n), limit, abort_flag); };
       auto issue_s = [&](int t, int j) {
-        const uint32_t q_base = smem_u32(sQ + t * kTileBytes), k_base = smem_u32(sK + (j & 1) * kTileBytes);
+        const uint32_t q_base = smem_u32(sQ + t * kTileBytes);
+        const uint32_t k_base = smem_u32(ring + ring_slot(2 * j) * kTileBytes);
 #pragma unroll
         for (int ds = 0; ds < kD / 16; ++ds) {
           const uint32_t off = (ds >> 2) * kChunk + (ds & 3) * 32;
@@ -275,7 +287,7 @@ __device__ __forceinline__ void producer_warps(const CUtensorMap& tm, const FwdP
         any = true;
       };
       auto issue_pv = [&](int t, int j) {
-        const uint32_t v_base = smem_u32(sV + (j & 1) * kTileBytes);
+        const uint32_t v_base = smem_u32(ring + ring_slot(2 * j + 1) * kTileBytes);
         const uint32_t p_tmem = tmem + t * 128;          // packed bf16 P in the first 64 S columns
         const uint32_t o_tmem = tmem + 256 + t * 128;
 #pragma unroll
@@ -286,29 +298,31 @@ __device__ __forceinline__ void producer_warps(const CUtensorMap& tm, const FwdP
         umma_commit(&o_done[t]);
       };
       if (ok && n_kv > 0) {
-        ok = mbar_wait(&kv_full[0], 0, limit, abort_flag);
+        ok = wait_slot(0);
         if (ok) {
           tc_fence_after();
           for (int t = 0; t < kQTiles; ++t) issue_s(t, 0);
+          umma_commit(&slot_empty[ring_slot(0)]);        // K_0 read by both S MMAs
         }
       }
       for (int j = 0; ok && j < n_kv; ++j) {
         const bool more = j + 1 < n_kv;
         for (int t = 0; t < kQTiles && ok; ++t) {
-          if (!mbar_wait(&p_full[t], j & 1, limit, abort_flag)) {
+          if (!mbar_wait(&p_full[t], j & 1, limit, abort_flag) || (t == 0 && !wait_slot(2 * j + 1))) {
             ok = false;
             break;
           }
           tc_fence_after();
           issue_pv(t, j);
-          if (t == kQTiles - 1) umma_commit(&kv_empty[j & 1]);
+          if (t == kQTiles - 1) umma_commit(&slot_empty[ring_slot(2 * j + 1)]);   // V_j consumed
           if (more) {
-            if (t == 0 && !mbar_wait(&kv_full[(j + 1) & 1], ((j + 1) >> 1) & 1, limit, abort_flag)) {
+            if (t == 0 && !wait_slot(2 * j + 2)) {
               ok = false;
               break;
             }
             tc_fence_after();
             issue_s(t, j + 1);
+            if (t == kQTiles - 1) umma_commit(&slot_empty[ring_slot(2 * j + 2)]);  // K_{j+1} consumed
           }
         }
       }
@@ -336,17 +350,16 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                        // kQTiles tiles
-  uint8_t* sK = sQ + kQTiles * kTileBytes;   // 2 stages
-  uint8_t* sV = sK + 2 * kTileBytes;         // 2 stages
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + 2 * kTileBytes);
+  uint8_t* ring = sQ + kQTiles * kTileBytes; // kSlots K/V slots
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + kSlots * kTileBytes);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;   // [2]
-  uint64_t* kv_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;    // [kQTiles]
-  uint64_t* p_full = bars + 7;    // [kQTiles]
-  uint64_t* o_done = bars + 9;    // [kQTiles]
-  uint64_t* drain = bars + 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* slot_full = bars + 1;                // [kSlots]
+  uint64_t* slot_empty = slot_full + kSlots;     // [kSlots]
+  uint64_t* s_full = slot_empty + kSlots;        // [kQTiles]
+  uint64_t* p_full = s_full + kQTiles;           // [kQTiles]
+  uint64_t* o_done = p_full + kQTiles;           // [kQTiles]
+  uint64_t* drain = o_done + kQTiles;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id(), lane = lane_id();
@@ -357,9 +370,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+    for (int i = 0; i < kSlots; ++i) {
+      mbar_init(&slot_full[i], 1);
+      mbar_init(&slot_empty[i], 1);
     }
     for (int t = 0; t < kQTiles; ++t) {
       mbar_init(&s_full[t], 1);
@@ -382,7 +395,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   if (warp < 4) {
     // Producer warpgroup: warp 0 TMA, warp 1 MMA issuer, warps 2-3 idle.
     setmaxnreg_dec<kRegsLow>();
-    producer_warps(tm, p, warp, sQ, sK, sV, q_full, kv_full, kv_empty, s_full, p_full, o_done, drain, abort_flag,
+    producer_warps(tm, p, warp, sQ, ring, q_full, slot_full, slot_empty, s_full, p_full, o_done, drain, abort_flag,
                    tmem, head, q0, n_kv, limit);
     tc_fence_before();
     named_bar_sync(1, kThreads);

@@ -72,16 +72,45 @@ def _pinned_empty(numel: int, dtype: torch.dtype) -> torch.Tensor:
     return _C.pinned_empty(numel, dtype)
 
 
+def _read_int(path: str) -> int | None:
+    try:
+        with open(path) as fh:
+            text = fh.read().strip()
+    except OSError:
+        return None
+    return None if not text or text == "max" else int(text)
+
+
+def cgroup_headroom_bytes() -> int | None:
+    """Bytes this process's memory cgroup may still take (None when unlimited or unknown).
+
+    A container's limit is invisible in /proc/meminfo, which reports the
+    whole machine; pinning past the cgroup limit gets the job killed.
+    """
+    for limit_path, usage_path in (("/sys/fs/cgroup/memory.max", "/sys/fs/cgroup/memory.current"),
+                                   ("/sys/fs/cgroup/memory/memory.limit_in_bytes",
+                                    "/sys/fs/cgroup/memory/memory.usage_in_bytes")):
+        limit = _read_int(limit_path)
+        if limit is None or limit >= 1 << 60:
+            continue
+        usage = _read_int(usage_path) or 0
+        return max(0, limit - usage)
+    return None
+
+
 def host_available_bytes() -> int:
-    """MemAvailable from /proc/meminfo (0 when unreadable)."""
+    """MemAvailable from /proc/meminfo, capped by the memory cgroup's headroom (0 when unreadable)."""
+    avail = 0
     try:
         with open("/proc/meminfo") as fh:
             for line in fh:
                 if line.startswith("MemAvailable:"):
-                    return int(line.split()[1]) * 1024
+                    avail = int(line.split()[1]) * 1024
+                    break
     except OSError:
         pass
-    return 0
+    headroom = cgroup_headroom_bytes()
+    return avail if headroom is None else min(avail, headroom)
 
 
 def choose_staging_target(requested: str, bytes_per_rank: int, local_ranks: int, device: torch.device) -> str:
