@@ -345,8 +345,6 @@ __device__ __forceinline__ void named_bar_sync(int id, int threads) {
 
 template <int POLY>
 __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_constant__ CUtensorMap tm, FwdParams p) {
-  constexpr uint32_t kIdescS = umma_idesc_bf16(kBQ, kBKV, false, false);
-  constexpr uint32_t kIdescPV = umma_idesc_bf16(kBQ, kD, false, true);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                        // kQTiles tiles
@@ -416,16 +414,12 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   float m_used = -INFINITY, l = 0.f;
   bool ok = true;
   for (int j = 0; j < n_kv; ++j) {
-    if (!mbar_wait(&s_full[t], j & 1, limit, abort_flag)) {
-      ok = false;
-      break;
-    }
     // O_t may be rescaled once PV_t of the previous tile completed (the
     // commit order already implies it: S_t(j) was issued after PV_t(j-1)).
-    if (j > 0 && !mbar_wait(&o_done[t], (j - 1) & 1, limit, abort_flag)) {
-      ok = false;
-      break;
-    }
+    // Warp-uniform outcome: tcgen05.ld/st below are warp-collective.
+    ok = __all_sync(0xffffffffu, mbar_wait(&s_full[t], j & 1, limit, abort_flag) &&
+                                     (j == 0 || mbar_wait(&o_done[t], (j - 1) & 1, limit, abort_flag)));
+    if (!ok) break;
     tc_fence_after();
     const int kv_valid = p.T - j * kBKV;
     // One TMEM read of the row; the max uses raw scores (the scale is positive).
@@ -465,7 +459,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     mbar_arrive(&p_full[t]);
   }
   const int q = q0 + t * kBQ + row;
-  if (ok && n_kv > 0 && mbar_wait(&o_done[t], (n_kv - 1) & 1, limit, abort_flag)) {
+  const bool done = __all_sync(0xffffffffu, ok && n_kv > 0 && mbar_wait(&o_done[t], (n_kv - 1) & 1, limit, abort_flag));
+  if (done) {
     tc_fence_after();
     const float inv_l = l > 0.f ? 1.f / l : 0.f;
 #pragma unroll

@@ -29,6 +29,7 @@
 
 #include <vector>
 
+#include "../common/gemv.cuh"
 #include "../common/ptx.cuh"
 #include "../gemm/gemm.h"
 #include "p2p.h"
@@ -327,33 +328,17 @@ struct AdalnParams {
 template <int R>
 __global__ void adaln_gather_kernel(AdalnParams p) {
   extern __shared__ float st[];
-  for (int i = threadIdx.x; i < R * p.K; i += blockDim.x) {
-    const float v = __bfloat162float(p.temb[i]);
-    st[i] = v / (1.f + __expf(-v));
-  }
-  __syncthreads();
+  silu_to_smem<R>(p.temb, p.K, st);
   const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
   const int ncols = p.world * p.rows;
   for (int n = blockIdx.x * warps + (threadIdx.x >> 5); n < p.rows; n += gridDim.x * warps) {
-    const __nv_bfloat16* wr = p.w + static_cast<long>(n) * p.K;
     float acc[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r) acc[r] = 0.f;
-    for (int k = lane * 8; k < p.K; k += 256) {
-      const uint4 u = *reinterpret_cast<const uint4*>(wr + k);
-      const __nv_bfloat16* wv = reinterpret_cast<const __nv_bfloat16*>(&u);
-#pragma unroll
-      for (int r = 0; r < R; ++r)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc[r] += __bfloat162float(wv[j]) * st[r * p.K + k + j];
-    }
+    warp_row_dot<R>(p.w + static_cast<long>(n) * p.K, st, p.K, acc);
+    const float bias = p.b != nullptr ? __bfloat162float(p.b[n]) : 0.f;
 #pragma unroll
     for (int r = 0; r < R; ++r) {
-      float v = acc[r];
-      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      v += p.b != nullptr ? __bfloat162float(p.b[n]) : 0.f;
       if (lane < p.world)  // lane `peer` stores the value into that rank's output
-        reinterpret_cast<float*>(p.out.p[lane])[static_cast<long>(r) * ncols + p.rank * p.rows + n] = v;
+        reinterpret_cast<float*>(p.out.p[lane])[static_cast<long>(r) * ncols + p.rank * p.rows + n] = acc[r] + bias;
     }
   }
 }
@@ -463,6 +448,7 @@ void adaln_project_gather(const at::Tensor& temb, const at::Tensor& w, const c10
   TORCH_CHECK(temb.scalar_type() == at::kBFloat16 && temb.is_contiguous() && w.is_contiguous(), "operands");
   const int R = static_cast<int>(temb.size(0)), K = static_cast<int>(temb.size(1));
   TORCH_CHECK(R >= 1 && R <= 2 && K % 8 == 0 && w.size(1) == K, "adaln_project_gather shapes");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(w.data_ptr()) & 15u) == 0, "weight rows must be 16-byte aligned");
   TORCH_CHECK(slot >= 3 && slot < 4, "signal slot 3 is reserved for the AdaLN gather");
   const int device = w.get_device();
   c10::cuda::CUDAGuard guard(device);
@@ -483,13 +469,17 @@ void adaln_project_gather(const at::Tensor& temb, const at::Tensor& w, const c10
   p.slot = static_cast<int>(slot);
   p.status = status_of(status, limit_ns);
   const size_t smem = static_cast<size_t>(R) * K * sizeof(float);
-  const int grid = std::min(p.rows / 8 + 1, 148 * 8);
+  auto go = [&](auto kernel) {
+    if (smem > 48 * 1024) cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    int per_sm = 1;   // persistent grid: as many blocks as fit at once
+    C10_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 256, smem));
+    const int grid = std::max(1, std::min((p.rows + 7) / 8, std::max(1, per_sm) * 148));
+    kernel<<<grid, 256, smem, stream>>>(p);
+  };
   if (R == 1) {
-    if (smem > 48 * 1024) cudaFuncSetAttribute(adaln_gather_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    adaln_gather_kernel<1><<<grid, 256, smem, stream>>>(p);
+    go(adaln_gather_kernel<1>);
   } else {
-    if (smem > 48 * 1024) cudaFuncSetAttribute(adaln_gather_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    adaln_gather_kernel<2><<<grid, 256, smem, stream>>>(p);
+    go(adaln_gather_kernel<2>);
   }
   adaln_signal_kernel<<<1, 32, 0, stream>>>(p);
   note_launch();

@@ -17,6 +17,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include "../common/gemv.cuh"
 #include "../common/ptx.cuh"
 #include "../gemm/gemm.h"
 #include "elementwise.h"
@@ -174,39 +175,23 @@ __global__ void rope_inverse_kernel(__nv_bfloat16* __restrict__ t, long ld, long
   }
 }
 
-// out[r, n] = sum_k silu(temb[r, k]) * W[n, k] + b[n]; one warp per output column n.
+// out[r, n] = sum_k silu(temb[r, k]) * W[n, k] + b[n]; one warp per output
+// column n at a time, persistent grid (rows strided over all warps).
 template <int R>
 __global__ void adaln_project_kernel(const __nv_bfloat16* __restrict__ temb, const __nv_bfloat16* __restrict__ w,
                                      const __nv_bfloat16* __restrict__ b, int N, int K, float* __restrict__ out) {
   extern __shared__ float st[];  // [R, K] silu(temb)
-  for (int i = threadIdx.x; i < R * K; i += blockDim.x) {
-    const float v = __bfloat162float(temb[i]);
-    st[i] = v / (1.f + __expf(-v));
-  }
-  __syncthreads();
+  silu_to_smem<R>(temb, K, st);
   const int warps = blockDim.x >> 5;
   const int lane = threadIdx.x & 31;
   for (int n = blockIdx.x * warps + (threadIdx.x >> 5); n < N; n += gridDim.x * warps) {
-    const __nv_bfloat16* wr = w + static_cast<long>(n) * K;
     float acc[R];
+    warp_row_dot<R>(w + static_cast<long>(n) * K, st, K, acc);
+    if (lane < R) {
+      float v = acc[0];
 #pragma unroll
-    for (int r = 0; r < R; ++r) acc[r] = 0.f;
-    for (int k = lane * 8; k < K; k += 32 * 8) {
-      float wv[8];
-      load8(wr + k, wv);
-#pragma unroll
-      for (int r = 0; r < R; ++r) {
-        const float* s = st + r * K + k;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc[r] += wv[j] * s[j];
-      }
-    }
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      float v = acc[r];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      if (lane == 0) out[static_cast<long>(r) * N + n] = v + (b != nullptr ? __bfloat162float(b[n]) : 0.f);
+      for (int r = 1; r < R; ++r) v = lane == r ? acc[r] : v;
+      out[static_cast<long>(lane) * N + n] = v + (b != nullptr ? __bfloat162float(b[n]) : 0.f);
     }
   }
 }
@@ -453,16 +438,21 @@ at::Tensor adaln_project(const at::Tensor& temb, const at::Tensor& w, const c10:
   const int R = static_cast<int>(temb.size(0));
   const int K = static_cast<int>(temb.size(1));
   TORCH_CHECK(w.size(1) == K && K % 8 == 0, "w must be [N, K]");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(w.data_ptr()) & 15u) == 0 && w.stride(0) == K,
+              "w rows must be contiguous and 16-byte aligned");
   TORCH_CHECK(R >= 1 && R <= 4, "adaln_project supports 1..4 timestep rows");
   c10::cuda::CUDAGuard guard(w.get_device());
   const int N = static_cast<int>(w.size(0));
   auto out = at::empty({R, N}, temb.options().dtype(at::kFloat));
   const size_t smem = static_cast<size_t>(R) * K * sizeof(float);
   const int threads = 256, warps = threads / 32;
-  const int grid = std::min(N / warps + 1, 148 * 8);
   const __nv_bfloat16* bp = b.has_value() ? reinterpret_cast<const __nv_bfloat16*>(b->data_ptr()) : nullptr;
   auto go = [&](auto kernel) {
     if (smem > 48 * 1024) cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    // persistent: as many blocks as fit on the SMs at once (shared memory bounds it)
+    int per_sm = 1;
+    C10_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem));
+    const int grid = std::max(1, std::min((N + warps - 1) / warps, std::max(1, per_sm) * 148));
     kernel<<<grid, threads, smem, cur_stream(w)>>>(reinterpret_cast<const __nv_bfloat16*>(temb.data_ptr()),
                                                    reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), bp, N, K,
                                                    out.data_ptr<float>());
