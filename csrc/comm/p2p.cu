@@ -329,16 +329,34 @@ template <int R>
 __global__ void adaln_gather_kernel(AdalnParams p) {
   extern __shared__ float st[];
   silu_to_smem<R>(p.temb, p.K, st);
+  constexpr int kRows = 4;
   const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
   const int ncols = p.world * p.rows;
-  for (int n = blockIdx.x * warps + (threadIdx.x >> 5); n < p.rows; n += gridDim.x * warps) {
-    float acc[R];
-    warp_row_dot<R>(p.w + static_cast<long>(n) * p.K, st, p.K, acc);
-    const float bias = p.b != nullptr ? __bfloat162float(p.b[n]) : 0.f;
+  const int groups = (p.rows + kRows - 1) / kRows;
+  for (int g = blockIdx.x * warps + (threadIdx.x >> 5); g < groups; g += gridDim.x * warps) {
+    const int n0 = g * kRows;
+    float acc[kRows][R];
+    if (n0 + kRows <= p.rows) {
+      warp_rows_dot<R, kRows>(p.w + static_cast<long>(n0) * p.K, st, p.K, acc);
+    } else {
+      for (int q = 0; q < kRows; ++q) {   // ragged last group: one row at a time
+        float one[1][R];
+        warp_rows_dot<R, 1>(p.w + static_cast<long>(min(n0 + q, p.rows - 1)) * p.K, st, p.K, one);
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
-      if (lane < p.world)  // lane `peer` stores the value into that rank's output
-        reinterpret_cast<float*>(p.out.p[lane])[static_cast<long>(r) * ncols + p.rank * p.rows + n] = acc[r] + bias;
+        for (int r = 0; r < R; ++r) acc[q][r] = one[0][r];
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < kRows; ++q) {
+      const int n = n0 + q;
+      if (n >= p.rows) break;
+      const float bias = p.b != nullptr ? __bfloat162float(p.b[n]) : 0.f;
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        if (lane < p.world)  // lane `peer` stores the value into that rank's output
+          reinterpret_cast<float*>(p.out.p[lane])[static_cast<long>(r) * ncols + p.rank * p.rows + n] =
+              acc[q][r] + bias;
+      }
     }
   }
 }
@@ -473,7 +491,7 @@ void adaln_project_gather(const at::Tensor& temb, const at::Tensor& w, const c10
     if (smem > 48 * 1024) cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     int per_sm = 1;   // persistent grid: as many blocks as fit at once
     C10_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 256, smem));
-    const int grid = std::max(1, std::min((p.rows + 7) / 8, std::max(1, per_sm) * 148));
+    const int grid = std::max(1, std::min((p.rows + 31) / 32, std::max(1, per_sm) * 148));
     kernel<<<grid, 256, smem, stream>>>(p);
   };
   if (R == 1) {

@@ -1,7 +1,9 @@
 // Weight-streaming GEMV helpers for the AdaLN projection: out[r, n] =
-// sum_k SiLU(temb[r, k]) * W[n, k].  Memory-bound (the weight is read once),
-// so each lane keeps four 16-byte weight loads in flight and the loads bypass
-// L1 (every weight byte is used exactly once).
+// sum_k SiLU(temb[r, k]) * W[n, k].  Memory-bound (the weight is read once):
+// a warp works on four rows at a time, so each lane keeps four 16-byte weight
+// loads in flight and reads each slice of the embedding from shared memory
+// once for all four rows; the loads bypass L1 (every weight byte is used
+// exactly once).
 #pragma once
 
 #include <cuda_bf16.h>
@@ -27,46 +29,46 @@ __device__ __forceinline__ void silu_to_smem(const __nv_bfloat16* __restrict__ t
   __syncthreads();
 }
 
-template <int R>
-__device__ __forceinline__ void fma8(const uint4& u, const float* st, int K, int k, float (&acc)[R]) {
-  const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&u);
-  float w[8];
+// One warp: the R dot products of ROWS consecutive weight rows starting at
+// `wr` (each K bf16, 16-byte aligned, row stride K) with the SiLU'd embedding
+// in smem; every lane returns the full sums.  Each 8-element slice of the
+// embedding is read from smem once and used for all ROWS rows.
+template <int R, int ROWS>
+__device__ __forceinline__ void warp_rows_dot(const __nv_bfloat16* __restrict__ wr, const float* st, int K,
+                                              float (&acc)[ROWS][R]) {
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const float2 f = __bfloat1622float2(w2[j]);
-    w[2 * j] = f.x;
-    w[2 * j + 1] = f.y;
-  }
+  for (int q = 0; q < ROWS; ++q)
 #pragma unroll
-  for (int r = 0; r < R; ++r) {
-    const float4 a = *reinterpret_cast<const float4*>(st + r * K + k);
-    const float4 b = *reinterpret_cast<const float4*>(st + r * K + k + 4);
-    acc[r] += w[0] * a.x + w[1] * a.y + w[2] * a.z + w[3] * a.w + w[4] * b.x + w[5] * b.y + w[6] * b.z + w[7] * b.w;
-  }
-}
-
-// One warp: the R dot products of weight row `wr` (K bf16, 16-byte aligned)
-// with the SiLU'd embedding in smem; every lane returns the full sums.
-template <int R>
-__device__ __forceinline__ void warp_row_dot(const __nv_bfloat16* __restrict__ wr, const float* st, int K,
-                                             float (&acc)[R]) {
-#pragma unroll
-  for (int r = 0; r < R; ++r) acc[r] = 0.f;
+    for (int r = 0; r < R; ++r) acc[q][r] = 0.f;
   const int lane = threadIdx.x & 31;
-  int k = lane * 8;
   constexpr int kStep = 32 * 8;   // elements one warp-wide 16-byte load covers
-  for (; k + 3 * kStep < K; k += 4 * kStep) {
-    uint4 u[4];
+  for (int k = lane * 8; k < K; k += kStep) {
+    uint4 u[ROWS];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) u[i] = ld_stream16(wr + k + i * kStep);
+    for (int q = 0; q < ROWS; ++q) u[q] = ld_stream16(wr + static_cast<long>(q) * K + k);
+    float4 a[R][2];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) fma8<R>(u[i], st, K, k + i * kStep, acc);
+    for (int r = 0; r < R; ++r) {
+      a[r][0] = *reinterpret_cast<const float4*>(st + r * K + k);
+      a[r][1] = *reinterpret_cast<const float4*>(st + r * K + k + 4);
+    }
+#pragma unroll
+    for (int q = 0; q < ROWS; ++q) {
+      const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&u[q]);
+      const float2 w01 = __bfloat1622float2(w2[0]), w23 = __bfloat1622float2(w2[1]);
+      const float2 w45 = __bfloat1622float2(w2[2]), w67 = __bfloat1622float2(w2[3]);
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+        acc[q][r] += w01.x * a[r][0].x + w01.y * a[r][0].y + w23.x * a[r][0].z + w23.y * a[r][0].w +
+                     w45.x * a[r][1].x + w45.y * a[r][1].y + w67.x * a[r][1].z + w67.y * a[r][1].w;
+    }
   }
-  for (; k < K; k += kStep) fma8<R>(ld_stream16(wr + k), st, K, k, acc);
 #pragma unroll
-  for (int r = 0; r < R; ++r)
+  for (int q = 0; q < ROWS; ++q)
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc[q][r] += __shfl_xor_sync(0xffffffffu, acc[q][r], o);
 }
 
 }  // namespace h3

@@ -182,16 +182,32 @@ __global__ void adaln_project_kernel(const __nv_bfloat16* __restrict__ temb, con
                                      const __nv_bfloat16* __restrict__ b, int N, int K, float* __restrict__ out) {
   extern __shared__ float st[];  // [R, K] silu(temb)
   silu_to_smem<R>(temb, K, st);
+  constexpr int kRows = 4;
   const int warps = blockDim.x >> 5;
   const int lane = threadIdx.x & 31;
-  for (int n = blockIdx.x * warps + (threadIdx.x >> 5); n < N; n += gridDim.x * warps) {
-    float acc[R];
-    warp_row_dot<R>(w + static_cast<long>(n) * K, st, K, acc);
-    if (lane < R) {
-      float v = acc[0];
+  const int groups = (N + kRows - 1) / kRows;
+  for (int g = blockIdx.x * warps + (threadIdx.x >> 5); g < groups; g += gridDim.x * warps) {
+    const int n0 = g * kRows;
+    float acc[kRows][R];
+    if (n0 + kRows <= N) {
+      warp_rows_dot<R, kRows>(w + static_cast<long>(n0) * K, st, K, acc);
+    } else {
+      for (int q = 0; q < kRows; ++q) {   // ragged last group: one row at a time
+        float one[1][R];
+        warp_rows_dot<R, 1>(w + static_cast<long>(min(n0 + q, N - 1)) * K, st, K, one);
 #pragma unroll
-      for (int r = 1; r < R; ++r) v = lane == r ? acc[r] : v;
-      out[static_cast<long>(lane) * N + n] = v + (b != nullptr ? __bfloat162float(b[n]) : 0.f);
+        for (int r = 0; r < R; ++r) acc[q][r] = one[0][r];
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < kRows; ++q) {
+      const int n = n0 + q;
+      if (n < N && lane < R) {
+        float v = acc[q][0];
+#pragma unroll
+        for (int r = 1; r < R; ++r) v = lane == r ? acc[q][r] : v;
+        out[static_cast<long>(lane) * N + n] = v + (b != nullptr ? __bfloat162float(b[n]) : 0.f);
+      }
     }
   }
 }
@@ -452,7 +468,7 @@ at::Tensor adaln_project(const at::Tensor& temb, const at::Tensor& w, const c10:
     // persistent: as many blocks as fit on the SMs at once (shared memory bounds it)
     int per_sm = 1;
     C10_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem));
-    const int grid = std::max(1, std::min((N + warps - 1) / warps, std::max(1, per_sm) * 148));
+    const int grid = std::max(1, std::min((N + 4 * warps - 1) / (4 * warps), std::max(1, per_sm) * 148));
     kernel<<<grid, threads, smem, cur_stream(w)>>>(reinterpret_cast<const __nv_bfloat16*>(temb.data_ptr()),
                                                    reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), bp, N, K,
                                                    out.data_ptr<float>());

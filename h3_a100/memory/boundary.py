@@ -210,6 +210,7 @@ class BoundaryStager:
         self.stats = stats
         self._stack: list[_Staged] = []
         self._stream = None
+        self.timeline = None    # optional StreamTimeline: copies on the "d2h" / "h2d" lanes
 
     def _copy_stream(self, device: torch.device):
         if device.type != "cuda":
@@ -230,7 +231,10 @@ class BoundaryStager:
         else:
             stream.wait_stream(torch.cuda.current_stream(tensor.device))
             with torch.cuda.stream(stream):
+                t0 = self.timeline.event(stream) if self.timeline is not None else None
                 slab.copy_(src.reshape(-1), non_blocking=True)
+                if t0 is not None:
+                    self.timeline.add("d2h", "boundary_d2h", t0, self.timeline.event(stream))
                 staged.d2h_done = torch.cuda.Event()
                 staged.d2h_done.record(stream)
             src.record_stream(stream)
@@ -254,7 +258,10 @@ class BoundaryStager:
             staged.upload = torch.empty(staged.slab.numel(), dtype=staged.dtype, device=staged.device)
             if staged.d2h_done is not None:
                 stream.wait_event(staged.d2h_done)
+            t0 = self.timeline.event(stream) if self.timeline is not None else None
             staged.upload.copy_(staged.slab, non_blocking=True)
+            if t0 is not None:
+                self.timeline.add("h2d", "boundary_h2d", t0, self.timeline.event(stream))
             staged.h2d_done = torch.cuda.Event()
             staged.h2d_done.record(stream)
 

@@ -40,6 +40,8 @@ class TorchComm:
         # Optional ``StallLedger``: when set, every wait of the compute stream
         # on a prefetched gather is timed as exposed all-gather time.
         self.ledger = None
+        # Optional ``StreamTimeline``: gathers are recorded on the "comm" lane.
+        self.timeline = None
 
     # ---------------- buffers ----------------
     def alloc_shard(self, numel: int, dtype: torch.dtype) -> torch.Tensor:
@@ -75,7 +77,10 @@ class TorchComm:
         self._stream.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(self._stream):
             out = self._buffer(total, shard.dtype)
+            t0 = self.timeline.event(self._stream) if self.timeline is not None else None
             self._all_gather_flat(out, shard)
+            if t0 is not None:
+                self.timeline.add("comm", "all_gather", t0, self.timeline.event(self._stream))
             event = torch.cuda.Event()
             event.record(self._stream)
         self.bytes_gathered += out.numel() * out.element_size()

@@ -122,7 +122,10 @@ class PeerComm(TorchComm):
         self._stream.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(self._stream):
             out = self._buffer(total, shard.dtype)
+            t0 = self.timeline.event(self._stream) if self.timeline is not None else None
             self.C.p2p_all_gather(self.peer_ptrs(shard), shard.numel() * shard.element_size(), out)
+            if t0 is not None:
+                self.timeline.add("comm", "all_gather_pull", t0, self.timeline.event(self._stream))
             event = torch.cuda.Event()
             event.record(self._stream)
         self.bytes_gathered += out.numel() * out.element_size()

@@ -66,6 +66,7 @@ class LoopMixin:
         """One matched cycle: Student x1, Fake x5 (reordered), then the contract checks."""
         self.matched_cycle_census.reset()
         self._begin_cycle_counters()
+        self.timeline.start_cycle()
         self.timer.start("student_step")
         with nvtx("h3/student_step"):
             dmd = self._student_step(samples)
@@ -76,9 +77,23 @@ class LoopMixin:
         self.timer.stop("critic_phase")
         values = torch.stack([dmd.reshape(()).float(), fake.reshape(()).float()]).cpu()
         self._record_cycle_times()
+        self._record_timeline(current_iter)
         if validate:
             self._validate_cycle(current_iter)
         return {"dmd": float(values[0]), "fake": float(values[1])}
+
+    def _record_timeline(self, current_iter: int) -> None:
+        """Lane unions of this cycle (and a Chrome trace) when ``H3_TIMELINE`` is set."""
+        if not self.timeline.enabled:
+            return
+        import os
+
+        rows = self.timeline.collect()
+        self.last_cycle_receipt["timeline"] = self.timeline.unions(rows)
+        path = os.path.join(self.timeline.out_dir, f"timeline_rank{pdist.get_rank():02d}_iter{current_iter:04d}.json")
+        self.timeline.write_chrome_trace(rows, path, pid=pdist.get_rank())
+        logger.info("[h3-a100][timeline] iter={} rank={} {}", current_iter, pdist.get_rank(),
+                    self.last_cycle_receipt["timeline"])
 
     def _record_cycle_times(self) -> None:
         """Per-phase device seconds and exposed (non-overlapped) collective time of this cycle.
@@ -119,11 +134,13 @@ class LoopMixin:
                     offload.begin_backward()
                 with self.model.adaln_scope(result["backward_key"]):
                     self.matched_cycle_census.note_backward(STUDENT_ROLE)
-                    (result["loss"] / self.gradient_accumulation_iters).backward()
+                    with self.timeline.span("compute", "student_backward"):
+                        (result["loss"] / self.gradient_accumulation_iters).backward()
                 self.residency("after_student_backward")
             running = running + result["dmd"] / self.gradient_accumulation_iters
         self.timer.start("optimizer_step")
-        opt.step(self.lr_schedulers[STUDENT].get_last_lr()[0])
+        with self.timeline.span("compute", "student_optimizer_step"):
+            opt.step(self.lr_schedulers[STUDENT].get_last_lr()[0])
         self.timer.stop("optimizer_step")
         self.lr_schedulers[STUDENT].step()
         opt.zero_grad()
@@ -166,11 +183,13 @@ class LoopMixin:
                     offload.begin_backward()
                 with self.model.adaln_scope(item.cache_key):
                     self.matched_cycle_census.note_backward(FAKE_ROLE)
-                    (loss / len(group)).backward()
+                    with self.timeline.span("compute", "fake_backward"):
+                        (loss / len(group)).backward()
             self.model.drop_adaln_key(item.cache_key)
             total = total + loss.detach() / len(group)
         self.timer.start("optimizer_step")
-        opt.step(self.lr_schedulers[FAKE].get_last_lr()[0])
+        with self.timeline.span("compute", "fake_optimizer_step"):
+            opt.step(self.lr_schedulers[FAKE].get_last_lr()[0])
         self.timer.stop("optimizer_step")
         self.lr_schedulers[FAKE].step()
         opt.zero_grad()

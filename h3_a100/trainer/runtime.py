@@ -78,9 +78,11 @@ class DMDRuntimeMixin:
 
     # ---------------------------------------------------------------- forwards
     def _predict(self, role: str, latents, sigmas, condition, key):
-        self.matched_cycle_census.note_forward(_LOGICAL[role], grad_enabled=bool(torch.is_grad_enabled()))
+        grad = bool(torch.is_grad_enabled())
+        self.matched_cycle_census.note_forward(_LOGICAL[role], grad_enabled=grad)
         timesteps = self._timesteps(sigmas)
-        return self.model.predict_velocity(role, latents, timesteps, condition, adaln_key=key)
+        with self.timeline.span("compute", f"{role}_forward{'_grad' if grad else ''}"):
+            return self.model.predict_velocity(role, latents, timesteps, condition, adaln_key=key)
 
     def _pair(self, fn, a, b):
         return fn(a[0], b[0], 0), (None if a[1] is None else fn(a[1], b[1], 1))

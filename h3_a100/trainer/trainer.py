@@ -28,6 +28,7 @@ from ..models.lora import FAKE, STUDENT
 from ..parallel import distributed as pdist
 from ..utils.log import logger
 from ..utils.memory import BlockResidencyProbe, ResidencyLogger, log_cuda_memory
+from ..utils.timeline import StreamTimeline
 from ..utils.timing import PhaseTimer, StallLedger
 from .checkpointing import CheckpointMixin
 from .loop import LoopMixin
@@ -146,6 +147,7 @@ class H3DmdTrainer(CheckpointMixin, LoopMixin, DMDRuntimeMixin):
         self.host_rng = torch.Generator().manual_seed(self.seed + pdist.get_rank())
         self.timer = PhaseTimer(enabled=True)
         self.stall_ledger = StallLedger()
+        self.timeline = StreamTimeline()
         self.residency = ResidencyLogger(self)
         self.metrics: list[dict] = []
         self.last_cycle_receipt: dict[str, Any] = {}
@@ -213,6 +215,8 @@ class H3DmdTrainer(CheckpointMixin, LoopMixin, DMDRuntimeMixin):
         model = self.model
         self.comm = comm or self._build_comm()
         self.comm.ledger = self.stall_ledger
+        if self.timeline.enabled:
+            self.comm.timeline = self.timeline
         pad = 4 * max(1, self.comm.world_size)
         model.prepare_shared_backbone(student_lora=self.student_lora_config, fake_lora=self.fake_lora_config,
                                       cache_enabled=self.adaln_cache_enabled,
@@ -250,6 +254,8 @@ class H3DmdTrainer(CheckpointMixin, LoopMixin, DMDRuntimeMixin):
                 pin_memory=self.boundary_offload_pin_memory, require_cuda=self.device.type == "cuda",
                 event_path=event_path)
             plan.attach_staging(self.boundary_staging)
+            if self.timeline.enabled:
+                self.boundary_staging.stager.timeline = self.timeline
         self.trainable_params = model.role_parameters(STUDENT)
         self.fake_trainable_params = model.role_parameters(FAKE)
         self._validate_shared_parameter_contract()
