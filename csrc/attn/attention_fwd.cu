@@ -69,8 +69,14 @@ struct FwdParams {
   float scale_log2;  // softmax scale * log2(e)
   __nv_bfloat16* o;
   float* lse;
+  // Diagnostic phase trace (null in normal runs): CTA (0, 0) records clock64
+  // at each phase of its MMA issuer and of the first lane band's softmax warp
+  // of each query tile, plus every softmax warp's P hand-off; kTraceSlots
+  // values per (tile, KV step).
+  long long* trace;
   KernelStatus status;
 };
+constexpr int kTraceSlots = 12;
 
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -271,6 +277,7 @@ __device__ __forceinline__ void producer_warps(const CUtensorMap& tm, const FwdP
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (elect_one()) {
+      long long* mtrace = (p.trace != nullptr && blockIdx.x == 0 && blockIdx.y == 0) ? p.trace : nullptr;
       bool any = false;
       bool ok = mbar_wait(q_full, 0, limit, abort_flag);
       auto wait_slot = [&](int n) { return mbar_wait(&slot_full[ring_slot(n)], ring_phase(n), limit, abort_flag); };
@@ -312,6 +319,7 @@ __device__ __forceinline__ void producer_warps(const CUtensorMap& tm, const FwdP
             ok = false;
             break;
           }
+          if (mtrace) mtrace[(static_cast<long>(t) * n_kv + j) * kTraceSlots + 6] = clock64();
           tc_fence_after();
           issue_pv(t, j);
           if (t == kQTiles - 1) umma_commit(&slot_empty[ring_slot(2 * j + 1)]);   // V_j consumed
@@ -322,6 +330,7 @@ __device__ __forceinline__ void producer_warps(const CUtensorMap& tm, const FwdP
             }
             tc_fence_after();
             issue_s(t, j + 1);
+            if (mtrace) mtrace[(static_cast<long>(t) * n_kv + j) * kTraceSlots + 7] = clock64();
             if (t == kQTiles - 1) umma_commit(&slot_empty[ring_slot(2 * j + 2)]);  // K_{j+1} consumed
           }
         }
@@ -413,19 +422,26 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   const uint32_t tO = tmem + 256 + t * 128 + lane_off;
   float m_used = -INFINITY, l = 0.f;
   bool ok = true;
+  long long* trace_band = (p.trace != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && lane == 0)
+                             ? p.trace + static_cast<long>(t) * n_kv * kTraceSlots
+                             : nullptr;
+  long long* trace = quarter == 0 ? trace_band : nullptr;
   for (int j = 0; j < n_kv; ++j) {
+    if (trace) trace[j * kTraceSlots + 0] = clock64();
     // O_t may be rescaled once PV_t of the previous tile completed (the
     // commit order already implies it: S_t(j) was issued after PV_t(j-1)).
     // Warp-uniform outcome: tcgen05.ld/st below are warp-collective.
     ok = __all_sync(0xffffffffu, mbar_wait(&s_full[t], j & 1, limit, abort_flag) &&
                                      (j == 0 || mbar_wait(&o_done[t], (j - 1) & 1, limit, abort_flag)));
     if (!ok) break;
+    if (trace) trace[j * kTraceSlots + 1] = clock64();
     tc_fence_after();
     const int kv_valid = p.T - j * kBKV;
     // One TMEM read of the row; the max uses raw scores (the scale is positive).
     uint32_t r[kBKV / 32][32];
     load_row(tS, r);
     if (kv_valid < kBKV) mask_row(r, kv_valid);
+    if (trace) trace[j * kTraceSlots + 2] = clock64();
     const float m_tile = row_max(r) * p.scale_log2;
     const float m_new = fmaxf(m_used, m_tile);
     const bool need = (j == 0) || (m_new > m_used + kRescaleThreshold);
@@ -435,11 +451,13 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       l *= alpha;
       m_used = m_new;
     }
+    if (trace) trace[j * kTraceSlots + 3] = clock64();
     tc_fence_after();
     // P = 2^(s*scale - m) as packed bf16 pairs over the consumed S columns.
     const float rowsum = kv_valid >= kBKV ? row_exp_pack<false, POLY>(tS, r, kv_valid, p.scale_log2, m_used)
                                           : row_exp_pack<true, POLY>(tS, r, kv_valid, p.scale_log2, m_used);
     l += rowsum;
+    if (trace) trace[j * kTraceSlots + 4] = clock64();
     // Rescale O_t after P is written (the S registers are dead by then, so
     // the O chunk does not push the row past the register budget); PV_t(j)
     // is issued only after p_full, i.e. after this.
@@ -457,6 +475,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     tmem_st_wait();
     tc_fence_before();
     mbar_arrive(&p_full[t]);
+    if (trace_band) trace_band[j * kTraceSlots + (quarter == 0 ? 5 : 7 + quarter)] = clock64();
   }
   const int q = q0 + t * kBQ + row;
   const bool done = __all_sync(0xffffffffu, ok && n_kv > 0 && mbar_wait(&o_done[t], (n_kv - 1) & 1, limit, abort_flag));
@@ -496,7 +515,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
 }  // namespace
 
 std::vector<at::Tensor> attention_fwd(const at::Tensor& qkv, int64_t heads, int64_t head_dim, const at::Tensor& status,
-                                      int64_t limit_ns) {
+                                      int64_t limit_ns, const c10::optional<at::Tensor>& trace) {
   TORCH_CHECK(qkv.is_cuda() && qkv.scalar_type() == at::kBFloat16 && qkv.dim() == 2 && qkv.stride(1) == 1,
               "qkv must be a 2-D CUDA bf16 tensor with unit column stride");
   TORCH_CHECK(head_dim == kD, "attention_fwd supports head_dim 128");
@@ -517,6 +536,13 @@ std::vector<at::Tensor> attention_fwd(const at::Tensor& qkv, int64_t heads, int6
   p.lse = lse.data_ptr<float>();
   p.status.word = status.data_ptr<int>();
   p.status.limit_ns = static_cast<uint64_t>(limit_ns);
+  p.trace = nullptr;
+  if (trace.has_value()) {
+    TORCH_CHECK(trace->is_cuda() && trace->scalar_type() == at::kLong &&
+                    trace->numel() >= static_cast<int64_t>(kQTiles) * p.n_kv * kTraceSlots,
+                "trace must be a CUDA int64 tensor of 2 * n_kv * ", kTraceSlots, " entries");
+    p.trace = reinterpret_cast<long long*>(trace->data_ptr<int64_t>());
+  }
   static bool configured[64] = {false};
   const int device = qkv.get_device();
   if (!configured[device]) {

@@ -14,7 +14,8 @@ int64_t pinned_bytes();
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "Hand-written sm_100a kernels of the H3 DMD trainer";
   m.def("gemm", &h3::gemm, "tcgen05 GEMM with fused epilogues");
-  m.def("attention_fwd", &h3::attention_fwd, "tcgen05 attention forward");
+  m.def("attention_fwd", &h3::attention_fwd, "tcgen05 attention forward", py::arg("qkv"), py::arg("heads"),
+        py::arg("head_dim"), py::arg("status"), py::arg("limit_ns"), py::arg("trace") = py::none());
   m.def("attention_bwd", &h3::attention_bwd, "tcgen05 attention backward");
   m.def("p2p_all_gather", &h3::p2p_all_gather, "pull all-gather over peer memory");
   m.def("lora_rs_adamw", &h3::lora_rs_adamw, "fused LoRA reduce-scatter + clip + AdamW + all-gather");
