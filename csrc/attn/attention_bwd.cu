@@ -68,8 +68,13 @@ struct BwdParams {
   float* dq_acc;           // [T, H] fp32
   __nv_bfloat16* dqkv;     // [T, 3H]
   int ablate;              // diagnostic only (H3_ATTN_BWD_ABLATE): 1 skip dQ adds, 2 skip exponentials
+  // Diagnostic phase trace (null in normal runs): CTA (0, 0) records clock64
+  // at each phase of query step i of warpgroup 0's first lane band and of the
+  // MMA issuer, kBwdTraceSlots values per step.
+  long long* trace;
   KernelStatus status;
 };
+constexpr int kBwdTraceSlots = 12;
 
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -270,6 +275,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (elect_one()) {
+      long long* mtrace = (p.trace != nullptr && blockIdx.x == 0 && blockIdx.y == 0) ? p.trace : nullptr;
       bool ok = mbar_wait(kv_full, 0, limit, abort_flag);
       bool any = false;
       const uint32_t k_base = smem_u32(sK), v_base = smem_u32(sV), ds_base = smem_u32(sDS);
@@ -294,7 +300,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         umma_commit(s_full);
         any = true;
+        if (mtrace) mtrace[i * kBwdTraceSlots + 10] = clock64();
         if (!mbar_wait(p_full, i & 1, limit, abort_flag)) { ok = false; break; }
+        if (mtrace) mtrace[i * kBwdTraceSlots + 11] = clock64();
         tc_fence_after();
         // dQ_i = dS K: A = dS (smem, rows = keys, queries contiguous: MN-major), B = K (MN-major), N = 64 halves.
 #pragma unroll
@@ -345,9 +353,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     bool ok = true;
     const bool reducer = quarter == 0 && lane == 0;   // issues this warpgroup's dQ reduces
+    long long* trace = (p.trace != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && half == 0 && reducer)
+                           ? p.trace : nullptr;
     for (int i = 0; i < n_q; ++i) {
       const int st = i & 1;
+      if (trace) trace[i * kBwdTraceSlots + 0] = clock64();
       if (!mbar_wait(s_full, i & 1, limit, abort_flag)) { ok = false; break; }
+      if (trace) trace[i * kBwdTraceSlots + 1] = clock64();
       tc_fence_after();
       const float* lse2 = reinterpret_cast<const float*>(sStage + st * kStageBytes + 2 * kTile);
       const float* delta = lse2 + kB;
@@ -358,6 +370,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld32(tDP + lane_off + (half * 2 + cc) * 32, rd[cc]);
       }
       tmem_ld_wait();
+      if (trace) trace[i * kBwdTraceSlots + 2] = clock64();
       if (half == 0) {
         asm volatile("bar.arrive 1, 256;" ::: "memory");
       } else {
@@ -405,6 +418,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(p_full);
+      if (trace) trace[i * kBwdTraceSlots + 4] = clock64();
       // dQ_i (rows = queries): this warpgroup's 64 columns as two 32-column fp32
       // boxes, staged in the 128B-swizzled layout in the stage that held Q_i
       // (warpgroup 0) or dO_i (warpgroup 1) -- free once the dV / dK MMAs read
@@ -416,8 +430,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         bulk_wait_read_all();
         mbar_arrive(&qd_empty[(i - 1) & 1]);
       }
+      if (trace) trace[i * kBwdTraceSlots + 5] = clock64();
       if (!mbar_wait(dq_full, i & 1, limit, abort_flag)) { ok = false; break; }
+      if (trace) trace[i * kBwdTraceSlots + 6] = clock64();
       if (!mbar_wait(&stage_read[st], (i >> 1) & 1, limit, abort_flag)) { ok = false; break; }
+      if (trace) trace[i * kBwdTraceSlots + 7] = clock64();
       tc_fence_after();
       if (!(p.ablate & 1)) {
         uint8_t* stage = sStage + st * kStageBytes + half * kTile;
@@ -439,6 +456,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         fence_async_smem();
         named_sync(2 + half, 128);
+        if (trace) trace[i * kBwdTraceSlots + 8] = clock64();
         if (reducer) {
           tma_reduce_add_2d(&tm_dq, stage, head * kD + half * 64, i * kB);
           tma_reduce_add_2d(&tm_dq, stage + kTile / 2, head * kD + half * 64 + 32, i * kB);
@@ -446,6 +464,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(dq_empty);
+      if (trace) trace[i * kBwdTraceSlots + 9] = clock64();
     }
     if (reducer) {
       bulk_wait_read_all();   // no reduce still reads this CTA's smem at exit
@@ -491,7 +510,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 }  // namespace
 
 at::Tensor attention_bwd(const at::Tensor& qkv, const at::Tensor& o, const at::Tensor& lse, const at::Tensor& dout,
-                         int64_t heads, int64_t head_dim, const at::Tensor& status, int64_t limit_ns) {
+                         int64_t heads, int64_t head_dim, const at::Tensor& status, int64_t limit_ns,
+                         const c10::optional<at::Tensor>& trace) {
   TORCH_CHECK(qkv.is_cuda() && qkv.scalar_type() == at::kBFloat16 && qkv.is_contiguous(), "qkv must be contiguous bf16");
   TORCH_CHECK(o.is_contiguous() && dout.is_contiguous() && o.scalar_type() == at::kBFloat16 &&
                   dout.scalar_type() == at::kBFloat16, "o and do must be contiguous bf16");
@@ -534,6 +554,13 @@ at::Tensor attention_bwd(const at::Tensor& qkv, const at::Tensor& o, const at::T
   if (const char* ab = std::getenv("H3_ATTN_BWD_ABLATE")) p.ablate = std::atoi(ab);
   p.status.word = status.data_ptr<int>();
   p.status.limit_ns = static_cast<uint64_t>(limit_ns);
+  p.trace = nullptr;
+  if (trace.has_value()) {
+    TORCH_CHECK(trace->is_cuda() && trace->scalar_type() == at::kLong &&
+                    trace->numel() >= static_cast<int64_t>(p.n_q) * kBwdTraceSlots,
+                "trace must be a CUDA int64 tensor of n_q * ", kBwdTraceSlots, " entries");
+    p.trace = reinterpret_cast<long long*>(trace->data_ptr<int64_t>());
+  }
   static bool configured[64] = {false};
   if (!configured[device]) {
     cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);

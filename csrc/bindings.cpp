@@ -16,7 +16,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &h3::gemm, "tcgen05 GEMM with fused epilogues");
   m.def("attention_fwd", &h3::attention_fwd, "tcgen05 attention forward", py::arg("qkv"), py::arg("heads"),
         py::arg("head_dim"), py::arg("status"), py::arg("limit_ns"), py::arg("trace") = py::none());
-  m.def("attention_bwd", &h3::attention_bwd, "tcgen05 attention backward");
+  m.def("attention_bwd", &h3::attention_bwd, "tcgen05 attention backward", py::arg("qkv"), py::arg("o"),
+        py::arg("lse"), py::arg("dout"), py::arg("heads"), py::arg("head_dim"), py::arg("status"),
+        py::arg("limit_ns"), py::arg("trace") = py::none());
   m.def("p2p_all_gather", &h3::p2p_all_gather, "pull all-gather over peer memory");
   m.def("lora_rs_adamw", &h3::lora_rs_adamw, "fused LoRA reduce-scatter + clip + AdamW + all-gather");
   m.def("adaln_project_gather", &h3::adaln_project_gather, "row-sharded AdaLN GEMV with fused output all-gather");

@@ -55,6 +55,30 @@ def main(argv=None) -> None:
         per["last_band_arrive_to_pv_issue"] = statistics.median(r[6] - max(r[5], r[8], r[9], r[10]) for r in rows)
         out[f"tile{tile}"] = per
     out["tile1_start_after_tile0"] = statistics.median(t[1][j][1] - t[0][j][1] for j in range(skip, n_kv - 1))
+    # backward: warpgroup 0's first lane band and the MMA issuer of CTA (0, 0)
+    do = torch.randn(args.tokens, h, device=dev).to(torch.bfloat16)
+    o, lse = _C.attention_fwd(qkv, args.heads, 128, status, int(10e9))
+    _C.attention_bwd(qkv, o, lse, do, args.heads, 128, status, int(10e9))    # warm-up
+    n_q = n_kv
+    bt = torch.zeros(n_q * 12, dtype=torch.int64, device=dev)
+    _C.attention_bwd(qkv, o, lse, do, args.heads, 128, status, int(10e9), bt)
+    torch.cuda.synchronize()
+    b = bt.view(n_q, 12).cpu().tolist()[skip:n_q - 1]
+    med = lambda f: statistics.median(f(r) for r in b)   # noqa: E731
+    bwd = {
+        "wait_s": med(lambda r: r[1] - r[0]),
+        "load_s_dp": med(lambda r: r[2] - r[1]),
+        "p_ds_compute_store": med(lambda r: r[4] - r[2]),
+        "prev_reduce_wait": med(lambda r: r[5] - r[4]),
+        "wait_dq": med(lambda r: r[6] - r[5]),
+        "wait_stage_read": med(lambda r: r[7] - r[6]),
+        "dq_stage": med(lambda r: r[8] - r[7]),
+        "reduce_issue_arrive": med(lambda r: r[9] - r[8]),
+        "step_period": statistics.median(y[1] - x[1] for x, y in zip(b, b[1:])),
+        "mma_sdp_issue_to_p_full": med(lambda r: r[11] - r[10]),
+        "dq_empty_to_next_sdp_issue": statistics.median(y[10] - x[9] for x, y in zip(b, b[1:])),
+    }
+    out["backward"] = bwd
     print(json.dumps(out, indent=1))
 
 
