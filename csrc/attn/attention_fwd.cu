@@ -512,302 +512,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   named_bar_sync(1, kThreads);
 }
 
-// ============================================================================
-// Single-tile variant: one 128-query tile per CTA, S double-buffered in TMEM,
-// two softmax warpgroups taking alternate KV steps.
-//
-// In the two-tile kernel above, a query tile's P is written over its own S
-// columns, so the tile's next S MMA has to wait for its PV MMA: every KV step
-// of a tile serialises softmax -> hand-off -> PV -> S (measured with the
-// phase trace: ~1,760 + ~350 + 1,024 cycles), and MUFU sits ~30 % idle.
-// Here the tile owns two S buffers (S_0, S_1) and one O:
-//   TMEM  S_0 [0,128)  S_1 [128,256)  O [256,384)   (P_b packed over S_b's first 64 columns)
-//   MMA order  S(0) S(1) | PV(0) S(2) | PV(1) S(3) | ...   S(j+2) only waits for PV(j)
-//   warps 4..7  softmax of even KV steps (buffer 0), warps 8..11 of odd steps (buffer 1)
-// so the softmax of step j+1 runs while step j's exponentials are still in
-// flight, and the exponentials (MUFU) become the limit they should be.  The
-// running row max passes between the two warpgroups through shared memory
-// (named barriers 2 / 3 alternate by step parity; the producer of m(j)
-// arrives, the consumer of m(j) syncs), each warpgroup keeps its own partial
-// row sum relative to the max it last saw, and the two partial sums are
-// combined once at the end.  O is rescaled (rarely: lazy threshold 2^8) by the
-// warpgroup whose step raised the max, after the previous PV finished.
-// Every named barrier is passed by every thread of both warpgroups in the
-// same order on all paths, including after a failed (bounded) wait.
-// ============================================================================
-constexpr int kSlots1 = 5;
-constexpr int kSmem1 = 1024 + kTileBytes * (1 + kSlots1) + 512 + 6 * kBQ * 4;  // Q, ring, barriers, exchange
-static_assert(kSmem1 <= 232448, "single-tile attention forward shared memory");
-
-template <int POLY>
-__global__ void __launch_bounds__(kThreads, 1) attn_fwd1_kernel(const __grid_constant__ CUtensorMap tm, FwdParams p) {
-  constexpr uint32_t kIdescS = umma_idesc_bf16(kBQ, kBKV, false, false);
-  constexpr uint32_t kIdescPV = umma_idesc_bf16(kBQ, kD, false, true);
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* ring = sQ + kTileBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + kSlots1 * kTileBytes);
-  uint64_t* q_full = bars;
-  uint64_t* slot_full = bars + 1;             // [kSlots1]
-  uint64_t* slot_empty = slot_full + kSlots1; // [kSlots1]
-  uint64_t* s_full = slot_empty + kSlots1;    // [2] per S buffer
-  uint64_t* p_full = s_full + 2;              // [2]
-  uint64_t* o_done = p_full + 2;              // [2] PV(j) commits o_done[j & 1]
-  uint64_t* o_final = o_done + 2;             // the last PV
-  uint64_t* drain = o_final + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* xm = reinterpret_cast<float*>(ring + kSlots1 * kTileBytes + 512);   // [2][kBQ] running max by step parity
-  float* xl = xm + 2 * kBQ;                                                  // [2][kBQ] final partial sums
-  float* xr = xl + 2 * kBQ;                                                  // [2][kBQ] their reference maxima
-
-  const int warp = warp_id(), lane = lane_id();
-  const int head = blockIdx.y;
-  const int q0 = blockIdx.x * kBQ;
-  const int n_kv = p.n_kv;
-  const uint64_t limit = p.status.limit_ns;
-
-  if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    for (int i = 0; i < kSlots1; ++i) {
-      mbar_init(&slot_full[i], 1);
-      mbar_init(&slot_empty[i], 1);
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&s_full[b], 1);
-      mbar_init(&p_full[b], 128);
-      mbar_init(&o_done[b], 1);
-    }
-    mbar_init(o_final, 1);
-    mbar_init(drain, 1);
-    *abort_flag = 0;
-    fence_barrier_init();
-  }
-  if (warp == 0 && lane == 0) tma_prefetch_desc(&tm);
-  if (warp == 1) {
-    tmem_alloc(tmem_slot, 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  const uint32_t tO = tmem + 256;
-
-  if (warp < 4) {
-    setmaxnreg_dec<kRegsLow>();
-    if (warp == 0 && elect_one()) {
-      // ---------------------------------------------------------- TMA producer
-      const int xq = head * kD, xk = p.H + head * kD, xv = 2 * p.H + head * kD;
-      mbar_arrive_expect_tx(q_full, kTileBytes);
-      tma_load_2d(sQ, &tm, q_full, xq, q0);
-      tma_load_2d(sQ + kChunk, &tm, q_full, xq + 64, q0);
-      int issued_phase[kSlots1];
-#pragma unroll
-      for (int s = 0; s < kSlots1; ++s) issued_phase[s] = -1;
-      for (int n = 0; n < 2 * n_kv && !*abort_flag; ++n) {
-        const int slot = n % kSlots1;
-        const uint32_t ph = static_cast<uint32_t>((n / kSlots1) & 1);
-        if (!mbar_wait(&slot_empty[slot], ph ^ 1u, limit, abort_flag)) {
-          report_status(p.status, kStatusTimeoutEmpty, n);
-          *abort_flag = 1;
-          break;
-        }
-        const int x = (n & 1) ? xv : xk, y = (n >> 1) * kBKV;
-        mbar_arrive_expect_tx(&slot_full[slot], kTileBytes);
-        tma_load_2d(ring + slot * kTileBytes, &tm, &slot_full[slot], x, y);
-        tma_load_2d(ring + slot * kTileBytes + kChunk, &tm, &slot_full[slot], x + 64, y);
-        issued_phase[slot] = static_cast<int>(ph);
-      }
-      volatile int never = 0;
-      mbar_wait(q_full, 0, limit, &never);
-      for (int s = 0; s < kSlots1; ++s)
-        if (issued_phase[s] >= 0) mbar_wait(&slot_full[s], issued_phase[s], limit, &never);
-    } else if (warp == 1 && elect_one()) {
-      // ---------------------------------------------------------- MMA issuer
-      bool any = false;
-      bool ok = mbar_wait(q_full, 0, limit, abort_flag);
-      auto wait_slot = [&](int n) {
-        return mbar_wait(&slot_full[n % kSlots1], static_cast<uint32_t>((n / kSlots1) & 1), limit, abort_flag);
-      };
-      const uint32_t q_base = smem_u32(sQ);
-      auto issue_s = [&](int j) {      // S(j) into buffer j & 1
-        const uint32_t k_base = smem_u32(ring + ((2 * j) % kSlots1) * kTileBytes);
-        const uint32_t d = tmem + (j & 1) * 128;
-#pragma unroll
-        for (int ds = 0; ds < kD / 16; ++ds) {
-          const uint32_t off = (ds >> 2) * kChunk + (ds & 3) * 32;
-          umma_f16_ss(d, umma_smem_desc(q_base + off, 16, 1024), umma_smem_desc(k_base + off, 16, 1024), kIdescS,
-                      ds > 0 ? 1u : 0u);
-        }
-        umma_commit(&s_full[j & 1]);
-        umma_commit(&slot_empty[(2 * j) % kSlots1]);
-        any = true;
-      };
-      for (int j = 0; ok && j < n_kv && j < 2; ++j) {
-        ok = wait_slot(2 * j);
-        if (ok) {
-          tc_fence_after();
-          issue_s(j);
-        }
-      }
-      for (int j = 0; ok && j < n_kv; ++j) {
-        const int b = j & 1;
-        if (!mbar_wait(&p_full[b], (j >> 1) & 1, limit, abort_flag) || !wait_slot(2 * j + 1)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t v_base = smem_u32(ring + ((2 * j + 1) % kSlots1) * kTileBytes);
-        const uint32_t p_tmem = tmem + b * 128;
-#pragma unroll
-        for (int ks = 0; ks < kBKV / 16; ++ks) {
-          umma_f16_ts(tO, p_tmem + ks * 8, umma_smem_desc(v_base + ks * 2048, kChunk, 1024), kIdescPV,
-                      (j > 0 || ks > 0) ? 1u : 0u);
-        }
-        umma_commit(&o_done[b]);
-        umma_commit(&slot_empty[(2 * j + 1) % kSlots1]);
-        if (j == n_kv - 1) umma_commit(o_final);
-        if (j + 2 < n_kv) {
-          if (!wait_slot(2 * j + 4)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          issue_s(j + 2);
-        }
-      }
-      if (!ok) {
-        report_status(p.status, kStatusTimeoutFull, blockIdx.x);
-        *abort_flag = 1;
-      }
-      if (any) {
-        umma_commit(drain);
-        volatile int never = 0;
-        mbar_wait(drain, 0, limit, &never);
-      }
-    }
-    tc_fence_before();
-    named_bar_sync(1, kThreads);
-    if (warp == 1) {
-      tc_fence_after();
-      tmem_dealloc(tmem, 512);
-    }
-    return;
-  }
-  setmaxnreg_inc<kRegsHigh>();
-  // ------------------------------------------------------------ softmax (two warpgroups, alternate KV steps)
-  const int w = (warp - 4) >> 2;           // 0: even steps / buffer 0, 1: odd steps / buffer 1
-  const int quarter = warp & 3;
-  const int row = quarter * 32 + lane;
-  const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-  const uint32_t tS = tmem + w * 128 + lane_off;
-  const uint32_t tOr = tO + lane_off;
-  float l_w = 0.f, m_w = -INFINITY;   // this warpgroup's partial row sum and the max it is relative to
-  bool ok = true;
-  for (int j = w; j < n_kv; j += 2) {
-    const bool ready = ok && mbar_wait(&s_full[w], (j >> 1) & 1, limit, abort_flag);
-    ok = __all_sync(0xffffffffu, ready);
-    const int kv_valid = p.T - j * kBKV;
-    uint32_t r[kBKV / 32][32];
-    float m_tile = -INFINITY;
-    if (ok) {
-      tc_fence_after();
-      load_row(tS, r);
-      if (kv_valid < kBKV) mask_row(r, kv_valid);
-      m_tile = row_max(r) * p.scale_log2;
-    }
-    // m(j-1) from the other warpgroup (always passed, also after a failure)
-    float m_prev = -INFINITY;
-    if (j > 0) {
-      named_bar_sync(2 + ((j - 1) & 1), 256);
-      m_prev = xm[((j - 1) & 1) * kBQ + row];
-    }
-    const float m_new = fmaxf(m_prev, m_tile);
-    const bool need = (j == 0) || (m_new > m_prev + kRescaleThreshold);
-    const float m_used = need ? m_new : m_prev;
-    if (j + 1 < n_kv) {
-      xm[(j & 1) * kBQ + row] = m_used;
-      asm volatile("bar.arrive %0, 256;" ::"r"(2 + (j & 1)) : "memory");
-    }
-    if (!ok) continue;
-    const bool warp_need = __any_sync(0xffffffffu, need) && j > 0;
-    // this warpgroup's partial sum follows the running max
-    if (m_w != m_used) {
-      l_w = m_w == -INFINITY ? 0.f : l_w * ex2(m_w - m_used);
-      m_w = m_used;
-    }
-    tc_fence_after();
-    l_w += kv_valid >= kBKV ? row_exp_pack<false, POLY>(tS, r, kv_valid, p.scale_log2, m_used)
-                            : row_exp_pack<true, POLY>(tS, r, kv_valid, p.scale_log2, m_used);
-    // PV(j-1) must have finished before O is touched; waited every step so
-    // the parity of o_done[1 - w] stays in step with this warpgroup.
-    if (j > 0) {
-      ok = __all_sync(0xffffffffu, mbar_wait(&o_done[w ^ 1], ((j - 1) >> 1) & 1, limit, abort_flag));
-      if (!ok) continue;
-      tc_fence_after();
-    }
-    if (warp_need) {
-      const float alpha = need ? ex2(m_prev - m_used) : 1.f;
-#pragma unroll
-      for (int c = 0; c < kD / 16; ++c) {
-        uint32_t o[16];
-        tmem_ld16(tOr + c * 16, o);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-        tmem_st16(tOr + c * 16, o);
-      }
-    }
-    tmem_st_wait();
-    tc_fence_before();
-    mbar_arrive(&p_full[w]);
-  }
-  // Combine the two partial sums (both warpgroups always get here).
-  xl[w * kBQ + row] = l_w;
-  xr[w * kBQ + row] = m_w;
-  named_bar_sync(4, 256);
-  const float l_o = xl[(w ^ 1) * kBQ + row], m_o = xr[(w ^ 1) * kBQ + row];
-  const float m_fin = fmaxf(m_w, m_o);
-  float l_row = 0.f;
-  if (m_fin != -INFINITY) {
-    l_row = (m_w == -INFINITY ? 0.f : l_w * ex2(m_w - m_fin)) + (m_o == -INFINITY ? 0.f : l_o * ex2(m_o - m_fin));
-  }
-  const int q = q0 + row;
-  const bool done = __all_sync(0xffffffffu, ok && n_kv > 0 && mbar_wait(o_final, 0, limit, abort_flag));
-  if (done) {
-    tc_fence_after();
-    const float inv_l = l_row > 0.f ? 1.f / l_row : 0.f;
-#pragma unroll
-    for (int c = 0; c < kD / 2 / 16; ++c) {
-      uint32_t r16[16];
-      tmem_ld16(tOr + w * (kD / 2) + c * 16, r16);
-      tmem_ld_wait();
-      if (q < p.T) {
-        uint4 a, b;
-        a.x = pack_bf16x2(__uint_as_float(r16[0]) * inv_l, __uint_as_float(r16[1]) * inv_l);
-        a.y = pack_bf16x2(__uint_as_float(r16[2]) * inv_l, __uint_as_float(r16[3]) * inv_l);
-        a.z = pack_bf16x2(__uint_as_float(r16[4]) * inv_l, __uint_as_float(r16[5]) * inv_l);
-        a.w = pack_bf16x2(__uint_as_float(r16[6]) * inv_l, __uint_as_float(r16[7]) * inv_l);
-        b.x = pack_bf16x2(__uint_as_float(r16[8]) * inv_l, __uint_as_float(r16[9]) * inv_l);
-        b.y = pack_bf16x2(__uint_as_float(r16[10]) * inv_l, __uint_as_float(r16[11]) * inv_l);
-        b.z = pack_bf16x2(__uint_as_float(r16[12]) * inv_l, __uint_as_float(r16[13]) * inv_l);
-        b.w = pack_bf16x2(__uint_as_float(r16[14]) * inv_l, __uint_as_float(r16[15]) * inv_l);
-        uint4* dst = reinterpret_cast<uint4*>(p.o + static_cast<long>(q) * p.H + head * kD + w * (kD / 2) + c * 16);
-        dst[0] = a;
-        dst[1] = b;
-      }
-    }
-    if (q < p.T && w == 0) p.lse[static_cast<long>(head) * p.T + q] = (m_fin + __log2f(l_row)) * 0.6931471805599453f;
-  } else if (n_kv > 0) {
-    if (lane == 0) report_status(p.status, kStatusTimeoutAccFull, blockIdx.x);
-    *abort_flag = 1;
-  }
-  tc_fence_before();
-  named_bar_sync(1, kThreads);
-}
-
 }  // namespace
 
 std::vector<at::Tensor> attention_fwd(const at::Tensor& qkv, int64_t heads, int64_t head_dim, const at::Tensor& status,
@@ -860,35 +564,8 @@ std::vector<at::Tensor> attention_fwd(const at::Tensor& qkv, int64_t heads, int6
     const char* v = std::getenv("H3_ATTN_FWD_POLY");
     return v != nullptr ? std::atoi(v) : 0;
   }();
-  cudaStream_t stream = at::cuda::getCurrentCUDAStream(device).stream();
-  // H3_ATTN_FWD_KERNEL=1: the single-tile, double-buffered-S kernel.
-  static const int variant = [] {
-    const char* v = std::getenv("H3_ATTN_FWD_KERNEL");
-    return v != nullptr ? std::atoi(v) : 0;
-  }();
-  if (variant == 1 && p.trace == nullptr) {
-    static bool configured1[64] = {false};
-    if (!configured1[device]) {
-      for (auto fn : {attn_fwd1_kernel<0>, attn_fwd1_kernel<2>}) {
-        cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem1);
-        cudaFuncAttributes attr{};
-        C10_CUDA_CHECK(cudaFuncGetAttributes(&attr, fn));
-        TORCH_CHECK(attr.numRegs == kLaunchRegs, "single-tile attention forward compiled with ", attr.numRegs,
-                    " registers per thread; the register split assumes ", kLaunchRegs);
-      }
-      configured1[device] = true;
-    }
-    dim3 grid1(static_cast<unsigned>((T + kBQ - 1) / kBQ), static_cast<unsigned>(heads));
-    if (poly == 2) {
-      attn_fwd1_kernel<2><<<grid1, kThreads, kSmem1, stream>>>(tm, p);
-    } else {
-      attn_fwd1_kernel<0><<<grid1, kThreads, kSmem1, stream>>>(tm, p);
-    }
-    note_launch();
-    C10_CUDA_KERNEL_LAUNCH_CHECK();
-    return {o, lse};
-  }
   dim3 grid(static_cast<unsigned>((T + kQTiles * kBQ - 1) / (kQTiles * kBQ)), static_cast<unsigned>(heads));
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream(device).stream();
   switch (poly) {
     case 4: attn_fwd_kernel<4><<<grid, kThreads, kSmem, stream>>>(tm, p); break;
     default: attn_fwd_kernel<0><<<grid, kThreads, kSmem, stream>>>(tm, p); break;
