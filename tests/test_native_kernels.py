@@ -293,6 +293,24 @@ def test_attention_forward_large_logits(K):
     K.check_status()
 
 
+def test_attention_forward_max_jumps_late(K):
+    """A key tile far past the first one (and the masked last tile) raises
+    some rows' max by much more than the lazy-rescale threshold, so O and the
+    row sum must be rescaled mid-sequence."""
+    torch.manual_seed(15)
+    t, heads, hd = 640, 2, 128
+    qkv = bf(t, 3 * heads * hd, scale=2.0).float()
+    h = heads * hd
+    qkv[384:512, h:2 * h] *= 4.0          # keys of KV tile 3
+    qkv[600:, h:2 * h] *= 6.0             # and of the masked last tile
+    qkv = qkv.to(torch.bfloat16)
+    o, lse = K.attention_fwd(qkv, heads, hd)
+    o_r, lse_r = R.attention_fwd(qkv.float(), heads, hd)
+    close(o, o_r, 3e-2)
+    close(lse, lse_r, 2e-3)
+    K.check_status()
+
+
 @pytest.mark.parametrize("t,heads", [(300, 2), (640, 1), (1000, 3)])
 def test_attention_backward_matches_oracle(K, t, heads):
     if not hasattr(K.C, "attention_bwd"):
