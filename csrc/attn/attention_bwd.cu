@@ -18,10 +18,12 @@
 //             dQ_i = dS K                               (smem A, MN-major), two
 //                    N = 64 halves in the TMEM columns S^T / dP^T leave free
 //             dV  += P^T dO_i,  dK += dS^T Q_i          (A from TMEM, .ts form)
-//           the same warps then read dQ_i out of TMEM (half of it each), stage
-//           it in the stage buffer whose Q_i / dO_i the dV/dK MMAs just finished
-//           reading, and add it into an fp32 accumulator with TMA bulk tensor
-//           reduce-adds (whole 128-byte lines; 16-byte red.add was slower).  The
+//           the same warps then read dQ_i out of TMEM into registers (half of
+//           it each) and release those TMEM columns to the next step's S^T /
+//           dP^T at once, then stage dQ_i in the stage buffer whose Q_i / dO_i
+//           the dV/dK MMAs just finished reading, and add it into an fp32
+//           accumulator with TMA bulk tensor reduce-adds (whole 128-byte
+//           lines; 16-byte red.add was slower).  The
 //           wait for the reduces' smem reads is deferred by one step (until
 //           after the next softmax), then the stage is handed back to the loader:
 //           waiting right away put the reduce latency on the critical path
@@ -433,24 +435,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (trace) trace[i * kBwdTraceSlots + 5] = clock64();
       if (!mbar_wait(dq_full, i & 1, limit, abort_flag)) { ok = false; break; }
       if (trace) trace[i * kBwdTraceSlots + 6] = clock64();
+      tc_fence_after();
+      // Read this warpgroup's 64 dQ columns into registers and hand the TMEM
+      // columns back at once: the next step's S^T / dP^T MMAs overwrite them,
+      // and must not wait for the staging buffer below (that wait put ~1,800
+      // cycles on every step's critical path).
+      uint32_t rq[2][32];
+      {
+        const uint32_t src = (half == 0 ? tS : tDP) + 64 + lane_off;
+        tmem_ld32(src, rq[0]);
+        tmem_ld32(src + 32, rq[1]);
+        tmem_ld_wait();
+      }
+      tc_fence_before();
+      mbar_arrive(dq_empty);
+      if (trace) trace[i * kBwdTraceSlots + 9] = clock64();
       if (!mbar_wait(&stage_read[st], (i >> 1) & 1, limit, abort_flag)) { ok = false; break; }
       if (trace) trace[i * kBwdTraceSlots + 7] = clock64();
-      tc_fence_after();
       if (!(p.ablate & 1)) {
         uint8_t* stage = sStage + st * kStageBytes + half * kTile;
-        const uint32_t src = (half == 0 ? tS : tDP) + 64 + lane_off;
 #pragma unroll
         for (int box = 0; box < 2; ++box) {
-          uint32_t r[32];
-          tmem_ld32(src + box * 32, r);
-          tmem_ld_wait();
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
             uint4 v;
-            v.x = r[u * 4];
-            v.y = r[u * 4 + 1];
-            v.z = r[u * 4 + 2];
-            v.w = r[u * 4 + 3];
+            v.x = rq[box][u * 4];
+            v.y = rq[box][u * 4 + 1];
+            v.z = rq[box][u * 4 + 2];
+            v.w = rq[box][u * 4 + 3];
             *reinterpret_cast<uint4*>(stage + box * (kTile / 2) + row * 128 + ((u ^ (row & 7)) << 4)) = v;
           }
         }
@@ -462,9 +474,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_reduce_add_2d(&tm_dq, stage + kTile / 2, head * kD + half * 64 + 32, i * kB);
         }
       }
-      tc_fence_before();
-      mbar_arrive(dq_empty);
-      if (trace) trace[i * kBwdTraceSlots + 9] = clock64();
     }
     if (reducer) {
       bulk_wait_read_all();   // no reduce still reads this CTA's smem at exit

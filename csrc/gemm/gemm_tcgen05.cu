@@ -19,6 +19,14 @@
 //   share both operand panels in L2.
 // * All waits are bounded (see ptx.cuh); on a timeout the kernel records an
 //   error code, drains its own TMA loads / MMAs, frees TMEM and returns.
+// * Pair mode (PAIR, the 256-column bf16 epilogues): a 2-CTA cluster computes
+//   one 256 x 256 tile with tcgen05.mma.cta_group::2 (M = 256).  Each CTA
+//   TMA-loads its own 128 rows of A and its own 128-row half of B into its
+//   own shared memory (plain loads, completing on the leader CTA's barrier),
+//   holds its 128 x 256 accumulator in its own TMEM and runs its own
+//   epilogue; the leader's single thread issues the MMAs for both, and its
+//   commits arrive on both CTAs' barriers.  Each SM thereby stages half of B
+//   per k-block (32 KB instead of 48 KB a stage).
 // * Every TMA load in this file targets one CTA only.
 #include <ATen/cuda/CUDAContext.h>
 #include <cstdlib>
@@ -86,11 +94,12 @@ struct GemmParams {
   KernelStatus status;
 };
 
-template <int BN>
+template <int BN, bool PAIR = false>
 struct Cfg {
-  static constexpr int kStages = (BN == 256) ? 4 : 6;
+  static constexpr int kBRows = PAIR ? BN / 2 : BN;   // rows of B this CTA stages per k-block
+  static constexpr int kStages = PAIR ? 6 : ((BN == 256) ? 4 : 6);
   static constexpr int kABytes = BM * BK * 2;
-  static constexpr int kBBytes = BN * BK * 2;
+  static constexpr int kBBytes = kBRows * BK * 2;
   static constexpr int kTmemCols = 2 * BN;
   // epilogue staging: 4 warps x 2 slots x (32 rows x 64 bf16 columns)
   static constexpr int kEpiSlotBytes = 32 * 64 * 2;
@@ -316,6 +325,67 @@ __device__ __forceinline__ void bulk_wait_read() {
 }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
+// ---------------------------------------------------------------- 2-CTA pair helpers
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Shared::cluster address of the same shared-memory object in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_to_rank(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// Tiled 2-D load into this CTA's shared memory whose completed bytes count on
+// the leader CTA's barrier (`bar_cluster`, a shared::cluster address).  Not a
+// multicast: the tile lands in this CTA only.
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, uint32_t bar_cluster, int x,
+                                                 int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void umma_f16_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                                 uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+// Arrive on the barrier at this offset in both CTAs of the pair once all
+// previously issued MMAs of this thread complete.
+__device__ __forceinline__ void umma_commit_pair_both(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .b16 m;\n\tmov.b16 m, 3;\n\t"
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n\t}" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit_pair_own(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols));
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::);
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols));
+}
+
 template <int EPI>
 __device__ __forceinline__ void epilogue16(const GemmParams& p, int m, int n, const uint32_t (&r)[16]) {
   const int valid = min(16, p.N - n);
@@ -391,16 +461,16 @@ __device__ __forceinline__ void epilogue16(const GemmParams& p, int m, int n, co
   }
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI>
+template <int BN, bool A_MN, bool B_MN, int EPI, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmA2a, const __grid_constant__ CUtensorMap tmA2b,
                 const __grid_constant__ CUtensorMap tmA2c, const __grid_constant__ CUtensorMap tmB2,
                 const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmOut2,
                 const __grid_constant__ CUtensorMap tmAux, const GemmParams p) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, PAIR>;
   constexpr int S = C::kStages;
-  constexpr uint32_t kIdesc = umma_idesc_bf16(BM, BN, A_MN, B_MN);
+  constexpr uint32_t kIdesc = umma_idesc_bf16(PAIR ? 2 * BM : BM, BN, A_MN, B_MN);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -424,7 +494,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 128);
+      mbar_init(&acc_empty[b], PAIR ? 8 : 128);   // pair: one arrive per epilogue warp of both CTAs
     }
     mbar_init(drain, 1);
     for (int i = 0; i < 8; ++i) mbar_init(&aux_full[i], 1);
@@ -440,16 +510,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, C::kTmemCols);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, C::kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, C::kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR) {
+    cluster_sync_all();   // both CTAs' barriers initialised before any load or commit reaches them
+  } else {
+    __syncthreads();
+  }
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const uint64_t limit = p.status.limit_ns;
   const int total_work = p.tiles_m * p.tiles_n * p.splits;
   const int total_kb = p.kb_main + p.kb_second;
+  // Pair mode: work units are 256-row tiles shared by the two CTAs of a
+  // cluster; rank 0 (the leader) issues the MMAs.
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const int unit0 = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int units = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+  const int m_mult = PAIR ? 2 : 1;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -459,10 +544,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t issued_phase[S];
       bool issued[S];
       for (int s = 0; s < S; ++s) issued[s] = false;
-      for (int work = blockIdx.x; work < total_work && !*abort_flag; work += gridDim.x) {
+      for (int work = unit0; work < total_work && !*abort_flag; work += units) {
         int m_blk, n_blk, ks;
         tile_coords(p, work, m_blk, n_blk, ks);
-        const int m0 = m_blk * BM, n0 = n_blk * BN;
+        const int m0 = (m_blk * m_mult + static_cast<int>(rank)) * BM;
+        const int n0 = n_blk * BN + static_cast<int>(rank) * C::kBRows;   // this CTA's rows of B
         const int kb_lo = ks * p.kb_per_split;
         const int kb_hi = min(total_kb, kb_lo + p.kb_per_split);
         const CUtensorMap* a2 = &tmA2a;
@@ -486,6 +572,30 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           uint8_t* a_dst = sA + stage * C::kABytes;
           uint8_t* b_dst = sB + stage * C::kBBytes;
+          if constexpr (PAIR) {
+            // Both CTAs' bytes count on the leader's barrier; only the leader arms it.
+            if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * (C::kABytes + C::kBBytes));
+            const uint32_t bar = map_to_rank(&full[stage], 0);
+            const int k0 = (kb < p.kb_main ? kb : kb - p.kb_main) * BK;
+            const CUtensorMap* ma_ = kb < p.kb_main ? &tmA : a2;
+            const CUtensorMap* mb_ = kb < p.kb_main ? &tmB : &tmB2;
+            tma_load_2d_pair(a_dst, ma_, bar, k0, m0);
+            if constexpr (!B_MN) {
+              tma_load_2d_pair(b_dst, mb_, bar, k0, n0);
+            } else {
+#pragma unroll
+              for (int c = 0; c < C::kBRows / 64; ++c) tma_load_2d_pair(b_dst + c * 8192, mb_, bar, n0 + c * 64, k0);
+            }
+            if (rank == 0) {
+              issued[stage] = true;
+              issued_phase[stage] = phase;
+            }
+            if (++stage == S) {
+              stage = 0;
+              phase ^= 1u;
+            }
+            continue;
+          }
           mbar_arrive_expect_tx(&full[stage], C::kABytes + C::kBBytes);
           if (kb < p.kb_main) {
             const int k0 = kb * BK;
@@ -572,14 +682,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (elect_one()) {
+    // ------------------------------------------------------------ MMA issuer (the leader's, in pair mode)
+    if (elect_one() && rank == 0) {
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool any = false;
-      for (int work = blockIdx.x; work < total_work && !*abort_flag; work += gridDim.x) {
+      for (int work = unit0; work < total_work && !*abort_flag; work += units) {
         int m_blk, n_blk, ks;
         tile_coords(p, work, m_blk, n_blk, ks);
         const int kb_lo = ks * p.kb_per_split;
@@ -608,23 +718,39 @@ __global__ void __launch_bounds__(kThreads, 1)
                                      : umma_smem_desc(a_base + kk * 32, 16, 1024);
             const uint64_t bd = B_MN ? umma_smem_desc(b_base + kk * 2048, 8192, 1024)
                                      : umma_smem_desc(b_base + kk * 32, 16, 1024);
-            umma_f16_ss(d_tmem, ad, bd, kIdesc, (kb > kb_lo || kk > 0) ? 1u : 0u);
+            if constexpr (PAIR) {
+              umma_f16_ss_pair(d_tmem, ad, bd, kIdesc, (kb > kb_lo || kk > 0) ? 1u : 0u);
+            } else {
+              umma_f16_ss(d_tmem, ad, bd, kIdesc, (kb > kb_lo || kk > 0) ? 1u : 0u);
+            }
           }
           any = true;
-          umma_commit(&empty[stage]);
+          if constexpr (PAIR) {
+            umma_commit_pair_both(&empty[stage]);
+          } else {
+            umma_commit(&empty[stage]);
+          }
           if (++stage == S) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        umma_commit(&acc_full[acc]);
+        if constexpr (PAIR) {
+          umma_commit_pair_both(&acc_full[acc]);
+        } else {
+          umma_commit(&acc_full[acc]);
+        }
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1u;
       }
       if (any) {
         // Wait for every issued MMA before TMEM can be released.
-        umma_commit(drain);
+        if constexpr (PAIR) {
+          umma_commit_pair_own(drain);
+        } else {
+          umma_commit(drain);
+        }
         volatile int never = 0;
         mbar_wait(drain, 0, limit, &never);
       }
@@ -637,9 +763,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t acc_phase = 0;
     int store_idx = 0;
     uint32_t aux_phase[2] = {0u, 0u};
-    for (int work = blockIdx.x; work < total_work; work += gridDim.x) {
+    // pair mode: the leader's accumulator-empty barrier, arrived on by one lane per warp of both CTAs
+    const uint32_t acc_empty_leader[2] = {PAIR ? map_to_rank(&acc_empty[0], 0) : 0u,
+                                          PAIR ? map_to_rank(&acc_empty[1], 0) : 0u};
+    for (int work = unit0; work < total_work; work += units) {
       int m_blk, n_blk, ks;
       tile_coords(p, work, m_blk, n_blk, ks);
+      m_blk = m_blk * m_mult + static_cast<int>(rank);   // this CTA's 128-row block
       if (!mbar_wait(&acc_full[acc], acc_phase, limit, abort_flag)) {
         if (lane == 0) report_status(p.status, kStatusTimeoutAccFull, work);
         *abort_flag = 1;
@@ -716,7 +846,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             store_idx += EPI == kEpiGelu ? 2 : 1;
           }
           tc_fence_before();
-          mbar_arrive(&acc_empty[acc]);
+          if constexpr (PAIR) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote(acc_empty_leader[acc]);
+          } else {
+            mbar_arrive(&acc_empty[acc]);
+          }
           acc ^= 1;
           if (acc == 0) acc_phase ^= 1u;
           continue;
@@ -735,7 +870,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(&acc_empty[acc]);
+      if constexpr (PAIR) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(acc_empty_leader[acc]);
+      } else {
+        mbar_arrive(&acc_empty[acc]);
+      }
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
@@ -743,10 +883,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR) {
+    // Neither CTA leaves while the other may still touch its barriers or TMEM.
+    cluster_sync_all();
+  } else {
+    __syncthreads();
+  }
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, C::kTmemCols);
+    if constexpr (PAIR) {
+      tmem_dealloc_pair(tmem_base, C::kTmemCols);
+    } else {
+      tmem_dealloc(tmem_base, C::kTmemCols);
+    }
   }
 }
 
@@ -791,19 +940,39 @@ int num_sms(int device) {
   return cached[device];
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI>
+template <int BN, bool A_MN, bool B_MN, int EPI, bool PAIR = false>
 void launch_variant(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& a2a, const CUtensorMap& a2b,
                     const CUtensorMap& a2c, const CUtensorMap& b2, const CUtensorMap& o1, const CUtensorMap& o2,
                     const CUtensorMap& aux, const GemmParams& p, int device, cudaStream_t stream) {
-  auto kernel = gemm_kernel<BN, A_MN, B_MN, EPI>;
+  auto kernel = gemm_kernel<BN, A_MN, B_MN, EPI, PAIR>;
+  constexpr int smem = Cfg<BN, PAIR>::kSmem;
+  static_assert(smem <= 232448, "GEMM shared memory");
   static bool configured[64] = {false};
   if (!configured[device]) {
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::kSmem);
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     configured[device] = true;
   }
   const int work = p.tiles_m * p.tiles_n * p.splits;
-  const int grid = std::min(work, num_sms(device));
-  kernel<<<grid, kThreads, Cfg<BN>::kSmem, stream>>>(a, b, a2a, a2b, a2c, b2, o1, o2, aux, p);
+  if constexpr (PAIR) {
+    // One 2-CTA cluster per 256-row tile in flight, persistent over tiles.
+    const int pairs = std::min(work, num_sms(device) / 2);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kernel, a, b, a2a, a2b, a2c, b2, o1, o2, aux, p));
+  } else {
+    const int grid = std::min(work, num_sms(device));
+    kernel<<<grid, kThreads, smem, stream>>>(a, b, a2a, a2b, a2c, b2, o1, o2, aux, p);
+  }
   g_launches.fetch_add(1, std::memory_order_relaxed);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -861,9 +1030,18 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, int64_
   TORCH_CHECK(!(a_mn && K2 > 0), "the second K-phase needs a K-major A");
 
   Operand oa = operand_of(A), ob = operand_of(B);
+  // 2-CTA pair mode for the 256-column bf16 epilogues on K-major A (no split-K,
+  // no fused gather); H3_GEMM_PAIR=0 turns it off for measurements.
+  static const bool pair_enabled = [] {
+    const char* v = std::getenv("H3_GEMM_PAIR");
+    return v == nullptr || std::atoi(v) != 0;
+  }();
+  const bool pair = pair_enabled && bn == 256 && !a_mn && epi != kEpiF32Acc && splits <= 1 && gather_src.empty() &&
+                    (b_mn ? (epi == kEpiBf16 || epi == kEpiGeluBwd) : true);
+  const int b_rows = pair ? bn / 2 : bn;   // rows of B one CTA stages (K-major B)
   // Stored shapes: K-major A = [M, K]; MN-major A = [K, M]; same for B with N.
   CUtensorMap ma = a_mn ? make_map(oa.ptr, oa.rows, oa.cols, oa.ld, 64) : make_map(oa.ptr, oa.rows, oa.cols, oa.ld, BM);
-  CUtensorMap mb = b_mn ? make_map(ob.ptr, ob.rows, ob.cols, ob.ld, 64) : make_map(ob.ptr, ob.rows, ob.cols, ob.ld, bn);
+  CUtensorMap mb = b_mn ? make_map(ob.ptr, ob.rows, ob.cols, ob.ld, 64) : make_map(ob.ptr, ob.rows, ob.cols, ob.ld, b_rows);
   CUtensorMap ma2[3] = {ma, ma, ma};
   CUtensorMap mb2 = mb;
   int kb_second = 0;
@@ -875,13 +1053,13 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, int64_
     }
     for (size_t i = A2.size(); i < 3; ++i) ma2[i] = ma2[0];
     Operand o2 = operand_of(*B2);
-    mb2 = b_mn ? make_map(o2.ptr, o2.rows, o2.cols, o2.ld, 64) : make_map(o2.ptr, o2.rows, o2.cols, o2.ld, bn);
+    mb2 = b_mn ? make_map(o2.ptr, o2.rows, o2.cols, o2.ld, 64) : make_map(o2.ptr, o2.rows, o2.cols, o2.ld, b_rows);
     kb_second = static_cast<int>((K2 + BK - 1) / BK);
   }
   GemmParams p{};
   p.M = static_cast<int>(M);
   p.N = static_cast<int>(N);
-  p.tiles_m = static_cast<int>((M + BM - 1) / BM);
+  p.tiles_m = static_cast<int>((M + (pair ? 2 * BM : BM) - 1) / (pair ? 2 * BM : BM));
   p.tiles_n = static_cast<int>((N + bn - 1) / bn);
   p.kb_main = static_cast<int>((K + BK - 1) / BK);
   p.kb_second = kb_second;
@@ -974,6 +1152,19 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, int64_
     p.tma_store = 1;
   }
 
+#define H3_GEMM_PAIR_CASE(AMN_, BMN_, EPI_)                                                   \
+  if (pair && a_mn == AMN_ && b_mn == BMN_ && epi == EPI_) {                                    \
+    launch_variant<256, AMN_, BMN_, EPI_, true>(ma, mb, ma2[0], ma2[1], ma2[2], mb2, mo, mo2, maux, p, device, stream); \
+    return;                                                                                     \
+  }
+  H3_GEMM_PAIR_CASE(false, false, kEpiBf16)
+  H3_GEMM_PAIR_CASE(false, false, kEpiRope)
+  H3_GEMM_PAIR_CASE(false, false, kEpiGelu)
+  H3_GEMM_PAIR_CASE(false, false, kEpiGatedRes)
+  H3_GEMM_PAIR_CASE(false, true, kEpiBf16)
+  H3_GEMM_PAIR_CASE(false, true, kEpiGeluBwd)
+#undef H3_GEMM_PAIR_CASE
+  TORCH_CHECK(!pair, "no pair-mode GEMM variant for b_mn=", b_mn, " epi=", epi);
 #define H3_GEMM_CASE(BN_, AMN_, BMN_, EPI_)                                                   \
   if (bn == BN_ && a_mn == AMN_ && b_mn == BMN_ && epi == EPI_) {                             \
     launch_variant<BN_, AMN_, BMN_, EPI_>(ma, mb, ma2[0], ma2[1], ma2[2], mb2, mo, mo2, maux, p, device, stream); \

@@ -71,9 +71,9 @@ def main(argv=None) -> None:
         "p_ds_compute_store": med(lambda r: r[4] - r[2]),
         "prev_reduce_wait": med(lambda r: r[5] - r[4]),
         "wait_dq": med(lambda r: r[6] - r[5]),
-        "wait_stage_read": med(lambda r: r[7] - r[6]),
+        "dq_tmem_read_release": med(lambda r: r[9] - r[6]),
+        "wait_stage_read": med(lambda r: r[7] - r[9]),
         "dq_stage": med(lambda r: r[8] - r[7]),
-        "reduce_issue_arrive": med(lambda r: r[9] - r[8]),
         "step_period": statistics.median(y[1] - x[1] for x, y in zip(b, b[1:])),
         "mma_sdp_issue_to_p_full": med(lambda r: r[11] - r[10]),
         "dq_empty_to_next_sdp_issue": statistics.median(y[10] - x[9] for x, y in zip(b, b[1:])),
