@@ -161,6 +161,7 @@ __global__ void all_gather_pull_kernel(PeerPtrs src, int world, long shard_bytes
 }
 
 // ------------------------------------------------------------------ LoRA RS + clip + AdamW + AG
+constexpr int kLoraScratchSlots = 16;   // scalar slots before the per-block partials
 struct LoraParams {
   PeerPtrs grad;    // fp32 [n_pad] per rank
   PeerPtrs param;   // bf16 [n_pad] per rank (replicated compute copy)
@@ -171,7 +172,7 @@ struct LoraParams {
   float* master;    // fp32 [chunk] (this rank's shard)
   float* m;
   float* v;
-  float* scratch;   // [0] local sum of squares, [1..kMaxRanks] peer partials, [15] norm
+  float* scratch;   // [0] local sum of squares, [15] norm, [16 + b] block b's partial sum of squares
   int* bar;         // grid barrier words
   long chunk;
   int world, rank, epoch;
@@ -240,11 +241,21 @@ __global__ void __launch_bounds__(256) lora_rs_adamw_kernel(LoraParams p) {
       }
     }
   }
+  // Each block's partial lands in its own slot and block 0 sums the slots in
+  // a fixed order (a float atomicAdd would make the norm, and so every
+  // parameter, depend on the order in which blocks arrive).
   ss = block_sum256(ss);
-  if (threadIdx.x == 0) atomicAdd(p.scratch, ss);
+  if (threadIdx.x == 0) p.scratch[kLoraScratchSlots + blockIdx.x] = ss;
   if (!grid_barrier(p.bar, p.status.limit_ns)) {
     if (threadIdx.x == 0) report_status(p.status, kStatusTimeoutPeer, 11);
     return;
+  }
+  if (blockIdx.x == 0) {
+    float part = 0.f;
+    for (int b = threadIdx.x; b < static_cast<int>(gridDim.x); b += blockDim.x)
+      part += __ldcg(p.scratch + kLoraScratchSlots + b);
+    part = block_sum256(part);
+    if (threadIdx.x == 0) p.scratch[0] = part;
   }
   // 3. exchange partial sums of squares -> global norm
   if (blockIdx.x == 0 && threadIdx.x == 0) {
@@ -428,6 +439,7 @@ void lora_rs_adamw(const std::vector<int64_t>& grad_ptrs, const std::vector<int6
   p.master = master.data_ptr<float>();
   p.m = m.data_ptr<float>();
   p.v = v.data_ptr<float>();
+  TORCH_CHECK(scratch.scalar_type() == at::kFloat && scratch.is_contiguous(), "scratch must be contiguous fp32");
   p.scratch = scratch.data_ptr<float>();
   p.bar = bar.data_ptr<int>();
   p.chunk = master.numel();
@@ -453,6 +465,8 @@ void lora_rs_adamw(const std::vector<int64_t>& grad_ptrs, const std::vector<int6
     grid_for_device[device] = std::max(1, std::min(per_sm, 4)) * sms;
   }
   const int grid = grid_for_device[device];
+  TORCH_CHECK(scratch.numel() >= kLoraScratchSlots + grid, "scratch needs ", kLoraScratchSlots + grid,
+              " floats (16 scalar slots + one partial per block)");
   void* args[] = {&p};
   const cudaError_t err = cudaLaunchCooperativeKernel(reinterpret_cast<void*>(lora_rs_adamw_kernel), grid, 256,
                                                       args, 0, stream);

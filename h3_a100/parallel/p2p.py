@@ -33,6 +33,9 @@ import torch.distributed as dist
 from .comm import TorchComm, _Pending
 
 SIGNAL_INTS = 64          # [4 slots x 8 senders] flags + 8 float slots
+# fused LoRA step scratch: 16 scalar slots ([15] = global gradient norm) + one
+# partial sum of squares per block of the cooperative grid (at most 8 per SM)
+LORA_SCRATCH_FLOATS = 16 + 8 * 160
 SLOT_ADALN = 3
 
 
@@ -59,7 +62,7 @@ class PeerComm(TorchComm):
         self.status = torch.zeros(4, dtype=torch.int32, device=self.device)
         self.limit_ns = int(30e9)
         self.bar = torch.zeros(2, dtype=torch.int32, device=self.device)
-        self.scratch = torch.zeros(16, dtype=torch.float32, device=self.device)
+        self.scratch = torch.zeros(LORA_SCRATCH_FLOATS, dtype=torch.float32, device=self.device)
         self.bytes_peer = 0
         # In-switch reduction (multimem) is opt-in: at 2 and 4 ranks the
         # unicast peer loads measured faster (1.15 vs 1.87 ms and 1.44 vs

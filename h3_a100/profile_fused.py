@@ -31,6 +31,8 @@ import json
 
 import torch
 
+from .parallel.p2p import LORA_SCRATCH_FLOATS
+
 OPS = ("weight_gather", "adaln_gather", "lora_step", "allgather_gemm")
 
 
@@ -100,7 +102,7 @@ def main(argv=None) -> None:
             grad = torch.randn(n, device=dev)
             param = torch.randn(n, device=dev).to(torch.bfloat16)
             master, m, v = param.float(), torch.zeros(n, device=dev), torch.zeros(n, device=dev)
-            scratch = torch.zeros(16, device=dev)
+            scratch = torch.zeros(LORA_SCRATCH_FLOATS, device=dev)
             bar = torch.zeros(2, dtype=torch.int32, device=dev)
             step = [0]
 

@@ -6,6 +6,8 @@ PyTorch fp32 statement of the op within tolerance."""
 import pytest
 import torch
 
+from h3_a100.parallel.p2p import LORA_SCRATCH_FLOATS
+
 pytestmark = pytest.mark.gpu
 
 
@@ -32,7 +34,7 @@ def test_lora_step_is_bitwise_deterministic_and_matches_adamw(C):
         param = param0.clone()
         master, m, v = param0.float(), torch.zeros(n, device="cuda"), torch.zeros(n, device="cuda")
         flags = torch.zeros(64, dtype=torch.int32, device="cuda")
-        scratch = torch.zeros(16, device="cuda")
+        scratch = torch.zeros(LORA_SCRATCH_FLOATS, device="cuda")
         bar = torch.zeros(2, dtype=torch.int32, device="cuda")
         st = _status()
         C.lora_rs_adamw([grad.data_ptr()], [param.data_ptr()], [flags.data_ptr()], 0, 1, master, m, v, scratch, bar,
