@@ -235,7 +235,6 @@ __device__ __forceinline__ uint32_t ring_phase(int n) { return static_cast<uint3
 
 // Producer warpgroup roles: warp 0 issues the TMA loads, warp 1 the MMAs.
 // Load sequence n = 0, 1, 2, ...: K_{n/2} for even n, V_{n/2} for odd n.
-template <bool SELF>
 __device__ __forceinline__ void producer_warps(const CUtensorMap& tm, const FwdParams& p, int warp, uint8_t* sQ,
                                                uint8_t* ring, uint64_t* q_full, uint64_t* slot_full,
                                                uint64_t* slot_empty, uint64_t* s_full, uint64_t* p_full,
@@ -275,7 +274,7 @@ __device__ __forceinline__ void producer_warps(const CUtensorMap& tm, const FwdP
       for (int s = 0; s < kSlots; ++s)
         if (issued_phase[s] >= 0) mbar_wait(&slot_full[s], issued_phase[s], limit, &never);
     }
-  } else if (warp == 1 && !SELF) {
+  } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (elect_one()) {
       long long* mtrace = (p.trace != nullptr && blockIdx.x == 0 && blockIdx.y == 0) ? p.trace : nullptr;
@@ -353,49 +352,7 @@ __device__ __forceinline__ void named_bar_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
-// Self-issue mode: one thread of query tile t's softmax warpgroup issues that
-// tile's MMAs itself right after the warpgroup's P is in TMEM (a named
-// barrier over its four warps), instead of handing P to a separate MMA
-// thread through an mbarrier.  Issues PV_t(j) (skipped for j < 0) and, when
-// j + 1 < n_kv, S_t(j+1); each tile commits once per K/V slot it read, so the
-// slot barriers count two arrivals.  Returns false if a tile wait timed out.
-__device__ __forceinline__ bool tile_issue(int t, int j, int n_kv, uint32_t tmem, uint8_t* sQ, uint8_t* ring,
-                                           uint64_t* slot_full, uint64_t* slot_empty, uint64_t* s_full,
-                                           uint64_t* o_done, uint64_t limit, volatile int* abort_flag) {
-  constexpr uint32_t kIdescS = umma_idesc_bf16(kBQ, kBKV, false, false);
-  constexpr uint32_t kIdescPV = umma_idesc_bf16(kBQ, kD, false, true);
-  if (j >= 0) {
-    const int n = 2 * j + 1;   // V_j
-    if (!mbar_wait(&slot_full[ring_slot(n)], ring_phase(n), limit, abort_flag)) return false;
-    tc_fence_after();
-    const uint32_t v_base = smem_u32(ring + ring_slot(n) * kTileBytes);
-    const uint32_t p_tmem = tmem + t * 128, o_tmem = tmem + 256 + t * 128;
-#pragma unroll
-    for (int ks = 0; ks < kBKV / 16; ++ks)
-      umma_f16_ts(o_tmem, p_tmem + ks * 8, umma_smem_desc(v_base + ks * 2048, kChunk, 1024), kIdescPV,
-                  (j > 0 || ks > 0) ? 1u : 0u);
-    umma_commit(&o_done[t]);
-    umma_commit(&slot_empty[ring_slot(n)]);
-  }
-  if (j + 1 < n_kv) {
-    const int n = 2 * (j + 1);   // K_{j+1}
-    if (!mbar_wait(&slot_full[ring_slot(n)], ring_phase(n), limit, abort_flag)) return false;
-    tc_fence_after();
-    const uint32_t q_base = smem_u32(sQ + t * kTileBytes);
-    const uint32_t k_base = smem_u32(ring + ring_slot(n) * kTileBytes);
-#pragma unroll
-    for (int ds = 0; ds < kD / 16; ++ds) {
-      const uint32_t off = (ds >> 2) * kChunk + (ds & 3) * 32;
-      umma_f16_ss(tmem + t * 128, umma_smem_desc(q_base + off, 16, 1024), umma_smem_desc(k_base + off, 16, 1024),
-                  kIdescS, ds > 0 ? 1u : 0u);
-    }
-    umma_commit(&s_full[t]);
-    umma_commit(&slot_empty[ring_slot(n)]);
-  }
-  return true;
-}
-
-template <int POLY, bool SELF>
+template <int POLY>
 __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_constant__ CUtensorMap tm, FwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -422,7 +379,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     mbar_init(q_full, 1);
     for (int i = 0; i < kSlots; ++i) {
       mbar_init(&slot_full[i], 1);
-      mbar_init(&slot_empty[i], SELF ? 2 : 1);   // self-issue: one commit per query tile
+      mbar_init(&slot_empty[i], 1);
     }
     for (int t = 0; t < kQTiles; ++t) {
       mbar_init(&s_full[t], 1);
@@ -445,7 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   if (warp < 4) {
     // Producer warpgroup: warp 0 TMA, warp 1 MMA issuer, warps 2-3 idle.
     setmaxnreg_dec<kRegsLow>();
-    producer_warps<SELF>(tm, p, warp, sQ, ring, q_full, slot_full, slot_empty, s_full, p_full, o_done, drain, abort_flag,
+    producer_warps(tm, p, warp, sQ, ring, q_full, slot_full, slot_empty, s_full, p_full, o_done, drain, abort_flag,
                    tmem, head, q0, n_kv, limit);
     tc_fence_before();
     named_bar_sync(1, kThreads);
@@ -469,19 +426,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
                              ? p.trace + static_cast<long>(t) * n_kv * kTraceSlots
                              : nullptr;
   long long* trace = quarter == 0 ? trace_band : nullptr;
-  // Self-issue mode: warp 7 issues query tile 0's MMAs and warp 10 tile 1's
-  // (lane quarters 3 and 2: away from the TMA warp's sub-partition).
-  const bool issuer_warp = SELF && warp == (t == 0 ? 7 : 10);
-  if (issuer_warp) {
-    if (elect_one()) {
-      if (!mbar_wait(q_full, 0, limit, abort_flag) ||
-          !tile_issue(t, -1, n_kv, tmem, sQ, ring, slot_full, slot_empty, s_full, o_done, limit, abort_flag)) {
-        report_status(p.status, kStatusTimeoutFull, blockIdx.x);
-        *abort_flag = 1;
-      }
-    }
-    __syncwarp();
-  }
   for (int j = 0; j < n_kv; ++j) {
     if (trace) trace[j * kTraceSlots + 0] = clock64();
     // O_t may be rescaled once PV_t of the previous tile completed (the
@@ -530,26 +474,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     }
     tmem_st_wait();
     tc_fence_before();
-    if constexpr (SELF) {
-      if (trace_band) trace_band[j * kTraceSlots + (quarter == 0 ? 5 : 7 + quarter)] = clock64();
-      named_bar_sync(2 + t, 128);   // the whole tile's P (and rescaled O) is in TMEM
-      if (issuer_warp) {
-        if (elect_one()) {
-          long long* mt = (p.trace != nullptr && blockIdx.x == 0 && blockIdx.y == 0) ? p.trace : nullptr;
-          if (mt) mt[(static_cast<long>(t) * n_kv + j) * kTraceSlots + 6] = clock64();
-          tc_fence_after();
-          if (!tile_issue(t, j, n_kv, tmem, sQ, ring, slot_full, slot_empty, s_full, o_done, limit, abort_flag)) {
-            report_status(p.status, kStatusTimeoutFull, blockIdx.x);
-            *abort_flag = 1;
-          }
-          if (mt) mt[(static_cast<long>(t) * n_kv + j) * kTraceSlots + 7] = clock64();
-        }
-        __syncwarp();
-      }
-    } else {
-      mbar_arrive(&p_full[t]);
-      if (trace_band) trace_band[j * kTraceSlots + (quarter == 0 ? 5 : 7 + quarter)] = clock64();
-    }
+    mbar_arrive(&p_full[t]);
+    if (trace_band) trace_band[j * kTraceSlots + (quarter == 0 ? 5 : 7 + quarter)] = clock64();
   }
   const int q = q0 + t * kBQ + row;
   const bool done = __all_sync(0xffffffffu, ok && n_kv > 0 && mbar_wait(&o_done[t], (n_kv - 1) & 1, limit, abort_flag));
@@ -620,7 +546,7 @@ std::vector<at::Tensor> attention_fwd(const at::Tensor& qkv, int64_t heads, int6
   static bool configured[64] = {false};
   const int device = qkv.get_device();
   if (!configured[device]) {
-    for (auto fn : {attn_fwd_kernel<0, false>, attn_fwd_kernel<4, false>, attn_fwd_kernel<0, true>}) {
+    for (auto fn : {attn_fwd_kernel<0>, attn_fwd_kernel<4>}) {
       cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
       // setmaxnreg.inc waits until the producer warpgroup has released enough
       // registers; that only balances if the launch count is the assumed one.
@@ -633,20 +559,17 @@ std::vector<at::Tensor> attention_fwd(const at::Tensor& qkv, int64_t heads, int6
   }
   // Exponentials: 0 = MUFU only, 4 = four of every 8 pairs on the FMA pipe
   // (measured slower at this issue rate; so was a packed bf16x2 MUFU form).
-  // H3_ATTN_FWD_POLY selects it for measurements only.  H3_ATTN_FWD_SELF=1
-  // lets each softmax warpgroup issue its own tile's MMAs.
+  // H3_ATTN_FWD_POLY selects it for measurements only.
   static const int poly = [] {
     const char* v = std::getenv("H3_ATTN_FWD_POLY");
     return v != nullptr ? std::atoi(v) : 0;
   }();
-  static const bool self_issue = [] {
-    const char* v = std::getenv("H3_ATTN_FWD_SELF");
-    return v != nullptr && std::atoi(v) != 0;
-  }();
   dim3 grid(static_cast<unsigned>((T + kQTiles * kBQ - 1) / (kQTiles * kBQ)), static_cast<unsigned>(heads));
   cudaStream_t stream = at::cuda::getCurrentCUDAStream(device).stream();
-  auto fn = self_issue ? attn_fwd_kernel<0, true> : (poly == 4 ? attn_fwd_kernel<4, false> : attn_fwd_kernel<0, false>);
-  fn<<<grid, kThreads, kSmem, stream>>>(tm, p);
+  switch (poly) {
+    case 4: attn_fwd_kernel<4><<<grid, kThreads, kSmem, stream>>>(tm, p); break;
+    default: attn_fwd_kernel<0><<<grid, kThreads, kSmem, stream>>>(tm, p); break;
+  }
   note_launch();
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {o, lse};
