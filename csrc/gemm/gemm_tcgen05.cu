@@ -1028,6 +1028,16 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, int64_
   const int bn = static_cast<int>(block_n);
   TORCH_CHECK(bn == 128 || bn == 256, "block_n must be 128 or 256");
   TORCH_CHECK(!(a_mn && K2 > 0), "the second K-phase needs a K-major A");
+  // The compiled variants (checked here, before any tensor map is built):
+  // K-major A with K-major B: every bf16 epilogue at block_n 256, plain bf16 at
+  // 128; K-major A with MN-major B: bf16 / GELU-backward at 256, bf16 at 128;
+  // MN-major A and B: the fp32 accumulate at either width.
+  const bool bf16_epi = epi == kEpiBf16 || epi == kEpiRope || epi == kEpiGelu || epi == kEpiGatedRes;
+  const bool variant_exists =
+      (!a_mn && !b_mn && ((bn == 256 && bf16_epi) || (bn == 128 && epi == kEpiBf16))) ||
+      (!a_mn && b_mn && ((bn == 256 && (epi == kEpiBf16 || epi == kEpiGeluBwd)) || (bn == 128 && epi == kEpiBf16))) ||
+      (a_mn && b_mn && epi == kEpiF32Acc);
+  TORCH_CHECK(variant_exists, "no GEMM variant for block_n=", bn, " a_mn=", a_mn, " b_mn=", b_mn, " epi=", epi);
 
   Operand oa = operand_of(A), ob = operand_of(B);
   // 2-CTA pair mode for the 256-column bf16 epilogues on K-major A (no split-K,
