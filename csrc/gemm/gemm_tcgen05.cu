@@ -1040,13 +1040,15 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, int64_
   TORCH_CHECK(variant_exists, "no GEMM variant for block_n=", bn, " a_mn=", a_mn, " b_mn=", b_mn, " epi=", epi);
 
   Operand oa = operand_of(A), ob = operand_of(B);
-  // 2-CTA pair mode for the 256-column bf16 epilogues on K-major A (no split-K,
-  // no fused gather); H3_GEMM_PAIR=0 turns it off for measurements.
+  // 2-CTA pair mode for the 256-column bf16 epilogues on K-major A (no
+  // split-K); with the fused gather every CTA still copies its 1/gridDim slice
+  // of each N-tile and each producer waits for the whole tile before loading
+  // its half.  H3_GEMM_PAIR=0 turns it off for measurements.
   static const bool pair_enabled = [] {
     const char* v = std::getenv("H3_GEMM_PAIR");
     return v == nullptr || std::atoi(v) != 0;
   }();
-  const bool pair = pair_enabled && bn == 256 && !a_mn && epi != kEpiF32Acc && splits <= 1 && gather_src.empty() &&
+  const bool pair = pair_enabled && bn == 256 && !a_mn && epi != kEpiF32Acc && splits <= 1 &&
                     (b_mn ? (epi == kEpiBf16 || epi == kEpiGeluBwd) : true);
   const int b_rows = pair ? bn / 2 : bn;   // rows of B one CTA stages (K-major B)
   // Stored shapes: K-major A = [M, K]; MN-major A = [K, M]; same for B with N.
