@@ -20,6 +20,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("lse"), py::arg("dout"), py::arg("heads"), py::arg("head_dim"), py::arg("status"),
         py::arg("limit_ns"), py::arg("trace") = py::none());
   m.def("p2p_all_gather", &h3::p2p_all_gather, "pull all-gather over peer memory");
+  m.def("p2p_all_gather_ce", &h3::p2p_all_gather_ce, "all-gather over peer memory on the copy engines");
   m.def("lora_rs_adamw", &h3::lora_rs_adamw, "fused LoRA reduce-scatter + clip + AdamW + all-gather");
   m.def("adaln_project_gather", &h3::adaln_project_gather, "row-sharded AdaLN GEMV with fused output all-gather");
   m.def("wait_flag_test", &h3::wait_flag_test, "bounded wait on a flag (failure-detection tests)");

@@ -9,6 +9,7 @@
 // the kernel returns); no kernel traps.  Peer memory is only read with
 // plain loads here; no TMA load reads another GPU's memory.
 //
+//   p2p_all_gather_ce    the same on the copy engines (one cudaMemcpyAsync per shard)
 //   p2p_all_gather       pull every rank's shard of a (static) buffer into a
 //                        local gathered copy; frozen weights need no flags
 //   lora_rs_adamw        per LoRA role, one cooperative kernel:
@@ -400,6 +401,24 @@ KernelStatus status_of(const at::Tensor& status, int64_t limit_ns) {
 }
 
 }  // namespace
+
+// The same all-gather on the copy engines: one cudaMemcpyAsync per owner's
+// shard (a peer address mapped into this process), in rank order on the
+// current stream.  No SM runs it, so a gather prefetched on a side stream
+// leaves every SM to the compute kernels it overlaps.
+void p2p_all_gather_ce(const std::vector<int64_t>& shard_ptrs, int64_t shard_bytes, const at::Tensor& out) {
+  TORCH_CHECK(out.is_cuda() && out.is_contiguous(), "out must be contiguous CUDA");
+  const int world = static_cast<int>(shard_ptrs.size());
+  TORCH_CHECK(out.numel() * out.element_size() >= shard_bytes * world, "out too small");
+  c10::cuda::CUDAGuard guard(out.get_device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream(out.get_device()).stream();
+  auto* dst = static_cast<uint8_t*>(out.data_ptr());
+  for (int r = 0; r < world; ++r) {
+    C10_CUDA_CHECK(cudaMemcpyAsync(dst + static_cast<long>(r) * shard_bytes,
+                                   reinterpret_cast<const void*>(shard_ptrs[r]), static_cast<size_t>(shard_bytes),
+                                   cudaMemcpyDeviceToDevice, stream));
+  }
+}
 
 void p2p_all_gather(const std::vector<int64_t>& shard_ptrs, int64_t shard_bytes, const at::Tensor& out) {
   TORCH_CHECK(out.is_cuda() && out.is_contiguous(), "out must be contiguous CUDA");

@@ -7,6 +7,7 @@
 namespace h3 {
 
 void p2p_all_gather(const std::vector<int64_t>& shard_ptrs, int64_t shard_bytes, const at::Tensor& out);
+void p2p_all_gather_ce(const std::vector<int64_t>& shard_ptrs, int64_t shard_bytes, const at::Tensor& out);
 void lora_rs_adamw(const std::vector<int64_t>& grad_ptrs, const std::vector<int64_t>& param_ptrs,
                    const std::vector<int64_t>& flag_ptrs, int64_t rank, int64_t epoch, const at::Tensor& master,
                    const at::Tensor& m, const at::Tensor& v, const at::Tensor& scratch, const at::Tensor& bar,

@@ -62,6 +62,56 @@ def _time(fn, iters: int, warmup: int = 3) -> float:
     return float(ms.item())
 
 
+def _interference(comm, shard, padded, K, cfg, args, lines, world) -> None:
+    """How much a prefetched frozen-weight gather slows the compute it hides
+    behind: the QKV GEMM of the sweep model timed alone, then while gathers of
+    one block's unit run back to back on the communication stream, once with
+    the pull kernel (SMs) and once on the copy engines (``gather_engine``)."""
+    from .models.shared_backbone import sequence_tokens
+
+    h = cfg.hidden
+    m_tok = sequence_tokens(_cfg_of(args))
+    x = (torch.randn(m_tok, h, device="cuda") * 0.5).to(torch.bfloat16)
+    w = (torch.randn(3 * h, h, device="cuda") * 0.02).to(torch.bfloat16)
+    iters = max(10, args.iters)
+
+    def gemm():
+        K.linear(x, w)
+
+    base = _time(gemm, iters)
+    result = {"op": "gather_interference", "impl": "p2p", "n_gpus": world, "gemm_alone_ms": round(base, 4),
+              "unit_bytes": padded * 2}
+    saved = comm.gather_engine
+    for engine in ("kernel", "copy"):
+        comm.gather_engine = engine
+
+        def gemm_under_gather():
+            # one gather of the unit per GEMM, issued first on the comm stream
+            out = comm.all_gather_async(shard, padded)
+            K.linear(x, w)
+            comm.recycle(comm.wait(out))
+
+        ms = _time(gemm_under_gather, iters)
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        g0.record(comm._stream)
+        for _ in range(5):
+            comm.recycle(comm.wait(comm.all_gather_async(shard, padded)))
+        g1.record(comm._stream)
+        torch.cuda.synchronize()
+        gather_alone = g0.elapsed_time(g1) / 5
+        result[f"gemm_with_{engine}_gather_ms"] = round(ms, 4)
+        result[f"{engine}_gather_alone_ms"] = round(gather_alone, 4)
+    comm.gather_engine = saved
+    lines.append(result)
+
+
+def _cfg_of(args):
+    from .config import load_config
+
+    return load_config(args.config)
+
+
 def main(argv=None) -> None:
     p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     p.add_argument("--config", default=os.path.join("configs", "h3_fused_collective_sweep.yaml"))
@@ -122,6 +172,8 @@ def main(argv=None) -> None:
         nbytes = padded * 2
         emit("weight_gather", impl, ms, hbm_bytes=nbytes + nbytes / world,
              link_bytes=nbytes * (world - 1) / world, extra={"unit_bytes": nbytes})
+        if impl == "p2p":
+            _interference(comm, shard, padded, K, cfg, args, lines, world)
 
         # ---- AdaLN projection (row-sharded) for two timestep rows
         rows = adaln_rows // world

@@ -4,8 +4,10 @@
 of the training step run in hand-written kernels (``csrc/comm/p2p.cu``) that
 read and write the other GPUs' memory directly:
 
-* frozen-weight shards live in symmetric buffers, so gathering a unit is a
-  pull kernel with no synchronisation at all (the shards never change);
+* frozen-weight shards live in symmetric buffers, so gathering a unit needs
+  no synchronisation at all (the shards never change): by default one
+  copy-engine memcpy per peer shard, which leaves every SM to the compute it
+  overlaps, or a pull kernel;
 * the AdaLN projection is computed on each rank's rows and the results are
   stored straight into every rank's output buffer (GEMV + all-gather fused);
 * each LoRA optimizer step is ONE cooperative kernel: reduce-scatter of the
@@ -68,6 +70,15 @@ class PeerComm(TorchComm):
         # unicast peer loads measured faster (1.15 vs 1.87 ms and 1.44 vs
         # 1.74 ms for a 198 M-parameter LoRA step).  H3_P2P_MULTIMEM=1 enables it.
         self.use_multimem = os.environ.get("H3_P2P_MULTIMEM", "0") == "1"
+        # Frozen-weight gathers run on the copy engines by default (one
+        # cudaMemcpyAsync per shard, no SM time): measured at 2 GPUs, a
+        # 226.5 MB gather overlapping the QKV GEMM slowed it by 1.9 % on the
+        # copy engines and by 9.6 % as the pull kernel (0.25 vs 0.21 ms for the
+        # gather alone, hidden behind the previous block either way).
+        # H3_P2P_GATHER=kernel selects the pull kernel.
+        self.gather_engine = os.environ.get("H3_P2P_GATHER", "copy")
+        if self.gather_engine not in ("kernel", "copy"):
+            raise ValueError(f"H3_P2P_GATHER must be kernel or copy, not {self.gather_engine!r}")
 
     # ---------------------------------------------------------------- buffers
     def alloc_symmetric(self, numel: int, dtype: torch.dtype) -> torch.Tensor:
@@ -126,7 +137,8 @@ class PeerComm(TorchComm):
         with torch.cuda.stream(self._stream):
             out = self._buffer(total, shard.dtype)
             t0 = self.timeline.event(self._stream) if self.timeline is not None else None
-            self.C.p2p_all_gather(self.peer_ptrs(shard), shard.numel() * shard.element_size(), out)
+            gather = self.C.p2p_all_gather_ce if self.gather_engine == "copy" else self.C.p2p_all_gather
+            gather(self.peer_ptrs(shard), shard.numel() * shard.element_size(), out)
             if t0 is not None:
                 self.timeline.add("comm", "all_gather_pull", t0, self.timeline.event(self._stream))
             event = torch.cuda.Event()
