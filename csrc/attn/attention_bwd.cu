@@ -42,6 +42,7 @@
 
 #include <cstdlib>
 
+#include "../common/extent.h"
 #include "../common/ptx.cuh"
 #include "../gemm/gemm.h"
 #include "attention.h"
@@ -74,6 +75,7 @@ struct BwdParams {
   // at each phase of query step i of warpgroup 0's first lane band and of the
   // MMA issuer, kBwdTraceSlots values per step.
   long long* trace;
+  long dqkv_extent;         // allocation extent, checked in the bounds-checked build only
   KernelStatus status;
 };
 constexpr int kBwdTraceSlots = 12;
@@ -484,13 +486,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const long key = k0 + row;
       const uint32_t src = (half == 0 ? tDV : tDK) + lane_off;
-      __nv_bfloat16* dst = p.dqkv + key * 3 * p.H + (half == 0 ? 2 : 1) * p.H + head * kD;
+      const long dst_off = key * 3 * p.H + (half == 0 ? 2 : 1) * p.H + head * kD;
+      __nv_bfloat16* dst = p.dqkv + dst_off;
 #pragma unroll
       for (int c = 0; c < kD / 32; ++c) {
         uint32_t r[32];
         tmem_ld32(src + c * 32, r);
         tmem_ld_wait();
-        if (key_valid) {
+        if (key_valid && H3_IN_BOUNDS(dst_off + c * 32, dst_off + c * 32 + 31, p.dqkv_extent, p.status)) {
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             uint4 v;
@@ -560,6 +563,7 @@ at::Tensor attention_bwd(const at::Tensor& qkv, const at::Tensor& o, const at::T
   p.delta = delta.data_ptr<float>();
   p.dq_acc = dq_acc.data_ptr<float>();
   p.dqkv = reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr());
+  p.dqkv_extent = extent_of(dqkv);
   if (const char* ab = std::getenv("H3_ATTN_BWD_ABLATE")) p.ablate = std::atoi(ab);
   p.status.word = status.data_ptr<int>();
   p.status.limit_ns = static_cast<uint64_t>(limit_ns);

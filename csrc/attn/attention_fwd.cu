@@ -35,6 +35,7 @@
 #include <cudaTypedefs.h>
 #include <torch/extension.h>
 
+#include "../common/extent.h"
 #include "../common/ptx.cuh"
 #include "../gemm/gemm.h"
 #include "attention.h"
@@ -74,6 +75,7 @@ struct FwdParams {
   // of each query tile, plus every softmax warp's P hand-off; kTraceSlots
   // values per (tile, KV step).
   long long* trace;
+  long o_extent, lse_extent;   // allocation extents, checked in the bounds-checked build only
   KernelStatus status;
 };
 constexpr int kTraceSlots = 12;
@@ -487,7 +489,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       uint32_t r[16];
       tmem_ld16(tO + c * 16, r);
       tmem_ld_wait();
-      if (q < p.T) {
+      const long o_off = static_cast<long>(q) * p.H + head * kD + c * 16;
+      if (q < p.T && H3_IN_BOUNDS(o_off, o_off + 15, p.o_extent, p.status)) {
         uint4 a, b;
         a.x = pack_bf16x2(__uint_as_float(r[0]) * inv_l, __uint_as_float(r[1]) * inv_l);
         a.y = pack_bf16x2(__uint_as_float(r[2]) * inv_l, __uint_as_float(r[3]) * inv_l);
@@ -497,12 +500,14 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         b.y = pack_bf16x2(__uint_as_float(r[10]) * inv_l, __uint_as_float(r[11]) * inv_l);
         b.z = pack_bf16x2(__uint_as_float(r[12]) * inv_l, __uint_as_float(r[13]) * inv_l);
         b.w = pack_bf16x2(__uint_as_float(r[14]) * inv_l, __uint_as_float(r[15]) * inv_l);
-        uint4* dst = reinterpret_cast<uint4*>(p.o + static_cast<long>(q) * p.H + head * kD + c * 16);
+        uint4* dst = reinterpret_cast<uint4*>(p.o + o_off);
         dst[0] = a;
         dst[1] = b;
       }
     }
-    if (q < p.T) p.lse[static_cast<long>(head) * p.T + q] = (m_used + __log2f(l)) * 0.6931471805599453f;
+    const long lse_off = static_cast<long>(head) * p.T + q;
+    if (q < p.T && H3_IN_BOUNDS(lse_off, lse_off, p.lse_extent, p.status))
+      p.lse[lse_off] = (m_used + __log2f(l)) * 0.6931471805599453f;
   } else if (n_kv > 0) {
     if (lane == 0) report_status(p.status, kStatusTimeoutAccFull, blockIdx.x);
     *abort_flag = 1;
@@ -534,6 +539,8 @@ std::vector<at::Tensor> attention_fwd(const at::Tensor& qkv, int64_t heads, int6
   p.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(head_dim)));
   p.o = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
   p.lse = lse.data_ptr<float>();
+  p.o_extent = extent_of(o);
+  p.lse_extent = extent_of(lse);
   p.status.word = status.data_ptr<int>();
   p.status.limit_ns = static_cast<uint64_t>(limit_ns);
   p.trace = nullptr;

@@ -24,6 +24,7 @@ enum StatusCode : int {
   kStatusTimeoutAccEmpty = 4,  // MMA waited for the epilogue
   kStatusTimeoutPeer = 5,      // cross-GPU flag never arrived
   kStatusBadArgument = 6,
+  kStatusOutOfBounds = 7,      // bounds-checked build: an access outside its allocation (skipped)
 };
 
 struct KernelStatus {
@@ -49,6 +50,25 @@ __device__ __forceinline__ void report_status(const KernelStatus& st, int code, 
     atomicAdd(st.word + 3, 1);
   }
 }
+
+// Bounds checks of the checked build (-DH3_BOUNDS_CHECK, extension
+// h3_a100._C_checked): H3_IN_BOUNDS(first, last, extent, st) is true when the
+// element offsets first..last lie inside an allocation of `extent` elements;
+// otherwise it records kStatusOutOfBounds (detail: the low 31 bits of the
+// offending offset) and the caller skips the access.  Only accesses whose
+// index arithmetic is this code's own are checked (TMA tensor maps bound
+// theirs in hardware).  In the normal build the macro is `true` and the
+// checks compile away.
+#ifdef H3_BOUNDS_CHECK
+__device__ __forceinline__ bool in_bounds(long first, long last, long extent, const KernelStatus& st) {
+  if (first >= 0 && last < extent) return true;
+  report_status(st, kStatusOutOfBounds, static_cast<int>((first < 0 ? first : last) & 0x7fffffff));
+  return false;
+}
+#define H3_IN_BOUNDS(first, last, extent, st) (::h3::in_bounds((first), (last), (extent), (st)))
+#else
+#define H3_IN_BOUNDS(first, last, extent, st) (true)
+#endif
 
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {

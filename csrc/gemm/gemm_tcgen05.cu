@@ -37,6 +37,7 @@
 #include <atomic>
 #include <mutex>
 
+#include "../common/extent.h"
 #include "../common/ptx.cuh"
 #include "gemm.h"
 
@@ -91,6 +92,9 @@ struct GemmParams {
   uint8_t* g_dst;
   int* g_flags;
   int ablate;     // diagnostic only (H3_GEMM_ABLATE): 1 = skip the epilogue's global stores
+  // allocation extents (elements; 16-byte units for g_dst / each g_src shard),
+  // checked in the bounds-checked build only
+  long out_extent, out2_extent, g_dst_units, g_src_units;
   KernelStatus status;
 };
 
@@ -395,7 +399,9 @@ __device__ __forceinline__ void epilogue16(const GemmParams& p, int m, int n, co
   for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
 
   if constexpr (EPI == kEpiF32Acc) {
-    float* dst = reinterpret_cast<float*>(p.out) + static_cast<long>(m) * p.ldo + n;
+    const long off = static_cast<long>(m) * p.ldo + n;
+    if (!H3_IN_BOUNDS(off, off + valid - 1, p.out_extent, p.status)) return;
+    float* dst = reinterpret_cast<float*>(p.out) + off;
     if (p.splits > 1) {
       for (int j = 0; j < valid; ++j) atomicAdd(dst + j, p.alpha * v[j]);
     } else {
@@ -410,7 +416,9 @@ __device__ __forceinline__ void epilogue16(const GemmParams& p, int m, int n, co
 #pragma unroll
       for (int j = 0; j < 16; ++j) bias[j] = 0.0f;
     }
-    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<long>(m) * p.ldo + n;
+    const long off = static_cast<long>(m) * p.ldo + n;
+    if (!H3_IN_BOUNDS(off, off + valid - 1, p.out_extent, p.status)) return;
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + off;
     if constexpr (EPI == kEpiBf16) {
 #pragma unroll
       for (int j = 0; j < 16; ++j) v[j] = p.alpha * v[j] + bias[j];
@@ -423,7 +431,9 @@ __device__ __forceinline__ void epilogue16(const GemmParams& p, int m, int n, co
         g[j] = gelu_tanh_f(v[j]);
       }
       store_row16_bf16(dst, v, valid);
-      store_row16_bf16(reinterpret_cast<__nv_bfloat16*>(p.out2) + static_cast<long>(m) * p.ldo2 + n, g, valid);
+      const long off2 = static_cast<long>(m) * p.ldo2 + n;
+      if (H3_IN_BOUNDS(off2, off2 + valid - 1, p.out2_extent, p.status))
+        store_row16_bf16(reinterpret_cast<__nv_bfloat16*>(p.out2) + off2, g, valid);
     } else if constexpr (EPI == kEpiRope) {
 #pragma unroll
       for (int j = 0; j < 16; ++j) v[j] = bf16_round(v[j] + bias[j]);
@@ -661,13 +671,16 @@ __global__ void __launch_bounds__(kThreads, 1)
               const long row = r0 + u / units_per_row;
               const int owner = static_cast<int>(row / p.g_rows);
               const long local = (row - owner * p.g_rows) * units_per_row + u % units_per_row;
-              v[k] = reinterpret_cast<const uint4*>(p.g_src[owner])[local];
+              v[k] = H3_IN_BOUNDS(local, local, p.g_src_units, p.status)
+                         ? reinterpret_cast<const uint4*>(p.g_src[owner])[local]
+                         : make_uint4(0u, 0u, 0u, 0u);
             }
           }
 #pragma unroll
           for (int k = 0; k < kU; ++k) {
             const long u = base + k * kGatherThreads;
-            if (u < u_hi) reinterpret_cast<uint4*>(p.g_dst)[r0 * units_per_row + u] = v[k];
+            if (u < u_hi && H3_IN_BOUNDS(r0 * units_per_row + u, r0 * units_per_row + u, p.g_dst_units, p.status))
+              reinterpret_cast<uint4*>(p.g_dst)[r0 * units_per_row + u] = v[k];
           }
         }
         // The tile is read by TMA (async proxy) in other CTAs: order this
@@ -1086,6 +1099,14 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, int64_
   p.group_m = 16;
   p.out = out.data_ptr();
   p.ldo = out.stride(0);
+  p.out_extent = extent_of(out);
+  p.out2_extent = out2.has_value() ? extent_of(*out2) : 0;
+#ifdef H3_BOUNDS_CHECK
+  // Test hook of the checked build: H3_BOUNDS_SHRINK=n pretends the output
+  // allocation is n elements shorter, so the checks must catch (and skip)
+  // the stores into its last n elements.
+  if (const char* shrink = std::getenv("H3_BOUNDS_SHRINK")) p.out_extent -= std::atol(shrink);
+#endif
   p.out2 = out2.has_value() ? out2->data_ptr() : nullptr;
   p.ldo2 = out2.has_value() ? out2->stride(0) : 0;
   p.bias = bias.has_value() ? reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr()) : nullptr;
@@ -1126,6 +1147,8 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, int64_
       p.g_src[i] = reinterpret_cast<const uint8_t*>(gather_src[i]);
     }
     p.g_dst = reinterpret_cast<uint8_t*>(const_cast<void*>(ob.ptr));
+    p.g_dst_units = extent_of(B) * 2 / 16;
+    p.g_src_units = gather_rows * K * 2 / 16;
     p.g_flags = gather_flags->data_ptr<int>();
     // slice counters start at zero every call (same stream, before the launch)
     C10_CUDA_CHECK(cudaMemsetAsync(p.g_flags, 0, sizeof(int) * p.tiles_n, stream));

@@ -36,7 +36,8 @@ EPI_BF16, EPI_GELU, EPI_ROPE = _C.EPI_BF16, _C.EPI_GELU, _C.EPI_ROPE
 EPI_GATED_RES, EPI_GELU_BWD, EPI_F32_ACC = _C.EPI_GATED_RES, _C.EPI_GELU_BWD, _C.EPI_F32_ACC
 STATUS_NAMES = {1: "timeout waiting for a TMA stage", 2: "timeout waiting for a free stage",
                 3: "timeout waiting for an accumulator", 4: "timeout waiting for the epilogue",
-                5: "timeout waiting for a peer GPU", 6: "bad argument"}
+                5: "timeout waiting for a peer GPU", 6: "bad argument",
+                7: "out-of-bounds access caught by the bounds-checked build"}
 
 
 def _num_sms(device: torch.device) -> int:
@@ -47,11 +48,13 @@ class NativeKernels:
     name = "native"
     native = True
 
-    def __init__(self, device: torch.device, *, wait_limit_s: float = 10.0) -> None:
+    def __init__(self, device: torch.device, *, wait_limit_s: float = 10.0, extension=None) -> None:
+        """``extension``: the compiled module to run (default ``h3_a100._C``;
+        tests pass ``h3_a100._C_checked``, the bounds-checked build)."""
         if device.type != "cuda":
             raise ValueError("NativeKernels needs a CUDA device")
         self.device = device
-        self.C = _C
+        self.C = extension if extension is not None else _C
         self.status = torch.zeros(4, dtype=torch.int32, device=device)
         self.limit_ns = int(wait_limit_s * 1e9)
         self.sms = _num_sms(device)

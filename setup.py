@@ -31,15 +31,40 @@ NVCC_FLAGS = [
     "-Xptxas", "-v" if os.environ.get("H3_PTXAS_VERBOSE") else "-O3",
 ]
 
+EXTENSIONS = [
+    CUDAExtension(
+        name="h3_a100._C",
+        sources=[os.path.join(ROOT, s) for s in SOURCES],
+        include_dirs=[os.path.join(ROOT, "csrc")],
+        extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
+    )
+]
+# H3_CHECKED_BUILD=1 also builds h3_a100._C_checked: the same kernels with
+# -DH3_BOUNDS_CHECK, where every global access whose index arithmetic is this
+# code's own is checked against its allocation and, if outside, skipped and
+# reported in the status word (tests/test_checked_build.py).
+CHECKED_SOURCES = [
+    "csrc/checked/checked_bindings.cpp",
+    "csrc/checked/checked_gemm_tcgen05.cu",
+    "csrc/checked/checked_elementwise.cu",
+    "csrc/checked/checked_attention_fwd.cu",
+    "csrc/checked/checked_attention_bwd.cu",
+    "csrc/checked/checked_p2p.cu",
+    "csrc/checked/checked_pinned_pool.cpp",
+]
+if os.environ.get("H3_CHECKED_BUILD", "0") == "1":
+    EXTENSIONS.append(
+        CUDAExtension(
+            name="h3_a100._C_checked",
+            sources=[os.path.join(ROOT, s) for s in CHECKED_SOURCES],
+            include_dirs=[os.path.join(ROOT, "csrc")],
+            extra_compile_args={"cxx": ["-O3", "-std=c++17", "-DH3_BOUNDS_CHECK"],
+                                "nvcc": NVCC_FLAGS + ["-DH3_BOUNDS_CHECK"]},
+        )
+    )
+
 setup(
     name="h3_a100_b200_ext",
-    ext_modules=[
-        CUDAExtension(
-            name="h3_a100._C",
-            sources=[os.path.join(ROOT, s) for s in SOURCES],
-            include_dirs=[os.path.join(ROOT, "csrc")],
-            extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
-        )
-    ],
+    ext_modules=EXTENSIONS,
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
 )
