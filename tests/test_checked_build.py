@@ -6,7 +6,8 @@ stores and fp32 accumulation, the fused gather's copies, the attention
 outputs) is checked against the real extent of its allocation, skipped if
 outside, and reported as status 7.  These tests run the kernels through it on
 ragged shapes and require (a) no report and (b) results equal to the normal
-build's bit for bit, and (c) that the checks do fire: with the output
+build's bit for bit (within rounding where fp32 atomics add in no fixed
+order), and (c) that the checks do fire: with the output
 allocation declared one row short (a host-side test hook), the last row must
 be reported and left unwritten.
 """
@@ -86,6 +87,8 @@ def test_checked_build_matches_normal_build(kernels):
     for key, v in ref.items():
         if key == "f32acc":   # split-K fp32 atomics: the summation order differs run to run
             torch.testing.assert_close(got[key], v, rtol=1e-5, atol=1e-4)
+        elif key == "attn_dqkv":   # dQ is summed over key tiles by TMA reduce-adds, in no fixed order
+            torch.testing.assert_close(got[key].float(), v.float(), rtol=1e-2, atol=1e-3)
         else:
             assert torch.equal(got[key], v), f"{key}: the checked build computes something else"
 
