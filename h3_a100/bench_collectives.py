@@ -5,7 +5,11 @@ configs/h3_fused_collective_sweep.yaml`` times, on every rank with CUDA events
 (after warm-up; the reported time is the max over ranks):
 
 * ``weight_gather``: one transformer block's frozen-weight unit, all-gathered
-  from the per-rank shards (NCCL ``all_gather_into_tensor`` vs the pull kernel);
+  from the per-rank shards (NCCL ``all_gather_into_tensor`` vs the peer-memory
+  gather: copy engines by default, ``H3_P2P_GATHER=kernel`` for the pull kernel);
+* ``gather_interference`` (p2p): the QKV GEMM timed alone and while a unit
+  gather runs beside it on the communication stream, with the pull kernel and
+  with the copy engines: what a hidden prefetch costs the compute;
 * ``adaln``: the row-sharded AdaLN projection of one block for the two
   timestep rows (GEMV on the local rows + NCCL all-gather of the outputs, vs
   the fused GEMV whose epilogue stores into every rank's output);
