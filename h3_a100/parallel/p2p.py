@@ -140,7 +140,8 @@ class PeerComm(TorchComm):
             gather = self.C.p2p_all_gather_ce if self.gather_engine == "copy" else self.C.p2p_all_gather
             gather(self.peer_ptrs(shard), shard.numel() * shard.element_size(), out)
             if t0 is not None:
-                self.timeline.add("comm", "all_gather_pull", t0, self.timeline.event(self._stream))
+                label = "all_gather_copy_engines" if self.gather_engine == "copy" else "all_gather_pull"
+                self.timeline.add("comm", label, t0, self.timeline.event(self._stream))
             event = torch.cuda.Event()
             event.record(self._stream)
         self.bytes_gathered += out.numel() * out.element_size()
